@@ -1,0 +1,434 @@
+"""Benchmark of the B200 attention hot path (KV write + paged decode attention).
+
+Contract: ``python bench.py --gpus N --steps K --warmup W`` prints ONE JSON line.
+For N > 1 it runs under torchrun, one process per GPU; the work is sharded by
+request with no collective on the data path (every rank owns its own KV pool
+and sequences), so ``scaling`` is "weak" and ``value`` aggregates all ranks.
+
+Default workload: decode, bf16, B=256 sequences per GPU,
+16 query heads / 8 KV heads, head_dim 128, 16-token pages, kv_len U[512,4096],
+random non-contiguous block tables over a 1.2x pool.  One step = the slot-mapped
+write of one new token per sequence (store_kvcache) + decode attention over the
+paged KV (split-KV kernel + split combine).  ``value`` is the step's
+algorithmic HBM bytes (K/V read once per kv head, q, out, tables, and the
+store's rows + slots) / step time.
+
+``--impl reference`` times the reference's CPU attention path (the oracle
+restatement, ``oracle/``) on the host cores instead, on a bounded sample of
+the same workload, and prints the same metric.  ``--workload`` selects other
+configurations for development measurements (prefill, mixed, long).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "nano-vllm-practice_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "paged decode attn HBM GB/s (% peak); chunked-prefill attn TFLOP/s; tok/s"
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"fvb_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(smax)), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _profile_traffic(kernel_key: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    p = REPO / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get(kernel_key)
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference attention path restated (oracle), on host cores
+# ---------------------------------------------------------------------------
+
+
+def cpu_decode_sample(batch, n_seqs: int, seed: int = 0):
+    """A bounded sample of a decode batch, copied to numpy fp32 (pages renumbered)."""
+    from femtovllm_b200 import workloads
+
+    rng = np.random.default_rng(seed)
+    seqs = sorted(rng.choice(batch.num_seqs, size=min(n_seqs, batch.num_seqs), replace=False).tolist())
+    sub = workloads.subset_for_oracle(batch, seqs)
+    sub["k_new"] = batch.k_new[seqs].float().cpu().numpy()
+    sub["v_new"] = batch.v_new[seqs].float().cpu().numpy()
+    sub["bytes"] = _decode_step_bytes(batch, seqs)
+    return sub
+
+
+def _decode_step_bytes(batch, seqs=None) -> int:
+    import torch
+
+    es = torch.finfo(batch.dtype).bits // 8
+    lens = batch.kv_lens if seqs is None else batch.kv_lens[seqs]
+    n = len(lens)
+    kv = 2 * int(lens.astype(np.int64).sum()) * batch.n_kv_heads * batch.head_dim * es
+    qo = 2 * n * batch.n_heads * batch.head_dim * es
+    tables = 4 * int(((lens + 15) // 16).sum()) + 4 * n
+    store = 2 * 2 * n * batch.n_kv_heads * batch.head_dim * es + 8 * n
+    return kv + qo + tables + store
+
+
+def cpu_decode_step(sub) -> None:
+    import oracle
+
+    kp, vp = sub["k_pool"], sub["v_pool"]
+    slots = oracle.build_slot_mapping(sub["positions"], np.arange(len(sub["kv_lens"])), sub["block_tables"])
+    oracle.store_kvcache(sub["k_new"], sub["v_new"], kp, vp, slots)
+    oracle.decode_attention(sub["q"], kp, vp, sub["block_tables"], sub["kv_lens"], acc_dtype=np.float32)
+
+
+def time_cpu_baseline(sub, steps: int, warmup: int) -> tuple[float, float]:
+    for _ in range(warmup):
+        cpu_decode_step(sub)
+    t = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        cpu_decode_step(sub)
+        t.append(time.perf_counter() - t0)
+    med = float(np.median(t))
+    return sub["bytes"] / med / 1e9, med
+
+
+def _blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+
+def run_gpu(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    from femtovllm_b200 import ops, workloads
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    batch = workloads.config2(seed=2 + rank).materialize(dev)
+    md = batch.device_metadata(dev)
+    q, kp, vp = batch.q, batch.k_pool, batch.v_pool
+    tables, lens, slots = md["block_tables"], md["kv_lens"], md["slot_mapping"]
+    max_kv = batch.max_kv_len
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ops.store_kvcache(batch.k_new, batch.v_new, kp, vp, slots)
+        return ops.paged_attention_gemv(q, kp, vp, tables, lens, max_kv)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # --- device-resident timing of whole steps ---
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    step_ms = ev0.elapsed_time(ev1) / args.steps
+
+    # --- the dominant kernel alone: decode attention launches (split + combine) ---
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    for _ in range(args.steps):
+        ops.paged_attention_gemv(q, kp, vp, tables, lens, max_kv)
+    d1.record(stream)
+    torch.cuda.synchronize()
+    decode_ms = d0.elapsed_time(d1) / args.steps
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        ops.store_kvcache(batch.k_new, batch.v_new, kp, vp, slots)
+    s1.record(stream)
+    torch.cuda.synchronize()
+    store_ms = s0.elapsed_time(s1) / args.steps
+
+    # --- end to end through the public API with host buffers ---
+    h_q = q.cpu().pin_memory()
+    h_k, h_v = batch.k_new.cpu().pin_memory(), batch.v_new.cpu().pin_memory()
+    h_tables, h_lens, h_slots = tables.cpu().pin_memory(), lens.cpu().pin_memory(), slots.cpu().pin_memory()
+    h_out = torch.empty_like(h_q).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_tables, h_lens, h_slots))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        dq = h_q.to(dev, non_blocking=True)
+        dk, dv = h_k.to(dev, non_blocking=True), h_v.to(dev, non_blocking=True)
+        dt, dl, ds = (h_tables.to(dev, non_blocking=True), h_lens.to(dev, non_blocking=True),
+                      h_slots.to(dev, non_blocking=True))
+        ops.store_kvcache(dk, dv, kp, vp, ds)
+        out = ops.paged_attention_gemv(dq, kp, vp, dt, dl, max_kv)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    step_bytes = _decode_step_bytes(batch)
+    decode_bytes = batch.decode_bytes()
+    res = {"step_ms": step_ms, "decode_ms": decode_ms, "store_ms": store_ms, "e2e_ms": e2e_ms,
+           "bytes": step_bytes, "tokens": batch.num_seqs}
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, res)
+    else:
+        gathered = [res]
+    clocks = clk.summary()
+    from femtovllm_b200 import capi
+
+    lib = capi.load()
+    plan_ws = lib.fvb_paged_attention_decode_workspace_size(batch.num_seqs, batch.n_heads, batch.n_kv_heads,
+                                                            batch.head_dim, max_kv)
+    launches_per_step = 2 + (1 if plan_ws > 0 else 0)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        sub = cpu_decode_sample(batch, args.cpu_seqs)
+        gbs, med = time_cpu_baseline(sub, steps=3, warmup=1)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": _blas_threads(), "kind": "port",
+               "sample": f"{len(sub['kv_lens'])} of {batch.num_seqs} config-2 sequences (store + decode), "
+                         f"fp32 numpy oracle, median of 3 steps ({med * 1e3:.1f} ms/step)"}
+    return gathered, clocks, decode_bytes, launches_per_step, cpu, (h2d, d2h), batch
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seqs", type=int, default=24)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    hbm_peak, tflops_peak, peak_src = _peaks()
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+    gathered, clocks, decode_bytes, launches, cpu, (h2d, d2h), batch = run_gpu(args, rank, world, local_rank)
+    if rank == 0:
+        t_step = max(g["step_ms"] for g in gathered)
+        t_e2e = max(g["e2e_ms"] for g in gathered)
+        t_dec = max(g["decode_ms"] for g in gathered)
+        total_bytes = sum(g["bytes"] for g in gathered)
+        tokens = sum(g["tokens"] for g in gathered)
+        value = total_bytes / (t_step * 1e-3) / 1e9
+        achieved = decode_bytes / (gathered[0]["decode_ms"] * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(t_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1)/sqrt(128) q/k/v, random non-contiguous block tables)",
+            "config": {
+                "workload": "config2: decode paged attention + 1-token store_kvcache per sequence",
+                "num_seqs_per_gpu": batch.num_seqs, "n_heads": batch.n_heads, "n_kv_heads": batch.n_kv_heads,
+                "head_dim": batch.head_dim, "block_size": 16, "kv_len": "U[512,4096]",
+                "pool_blocks_per_gpu": batch.num_blocks, "parallelism": f"request-sharded x{world}, no collective",
+                "l2": "inputs larger than L2 (K/V ~2.4 GB per GPU), no flush",
+            },
+            "tokens_per_s": round(tokens / (t_step * 1e-3), 1),
+            "pct_hbm_peak": round(100 * value / (hbm_peak * world), 2),
+            "kernel_ms": {"decode_attention": round(t_dec, 5), "store_kvcache": round(gathered[0]["store_ms"], 5)},
+            "roofline": {
+                "kernel": "decode attention (decode_split_kernel + decode_combine_kernel)",
+                "bound": "hbm",
+                "achieved": round(achieved, 1),
+                "peak": hbm_peak,
+                "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4),
+                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
+                "traffic": _profile_traffic("decode_config2"),
+            },
+            "cpu_baseline": cpu,
+            "e2e": {
+                "value": round(total_bytes / (t_e2e * 1e-3) / 1e9, 2),
+                "unit": "GB/s",
+                "ms_per_step": round(t_e2e, 5),
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "api": "femtovllm_b200.ops.store_kvcache + paged_attention_gemv from pinned host buffers",
+            },
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_arm(args, rank: int, world: int):
+    """The reference's CPU attention path (oracle restatement) on host cores."""
+    if rank != 0:
+        return
+    import torch
+
+    from femtovllm_b200 import workloads
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    batch = workloads.config2(seed=2)
+    # Host copy of only the sampled sequences' pages: draw the pools on the CPU.
+    rng = np.random.default_rng(0)
+    seqs = sorted(rng.choice(batch.num_seqs, size=min(args.cpu_seqs, batch.num_seqs), replace=False).tolist())
+    small = workloads.custom(batch.kv_lens[seqs], np.ones(len(seqs)), batch.n_heads, batch.n_kv_heads,
+                             batch.head_dim, torch.bfloat16, seed=2, pool_factor=1.2, qkv_scale=batch.qkv_scale)
+    small.materialize("cpu")
+    sub = workloads.subset_for_oracle(small, list(range(len(seqs))))
+    sub["k_new"] = small.k_new.float().numpy()
+    sub["v_new"] = small.v_new.float().numpy()
+    sub["bytes"] = _decode_step_bytes(small)
+    for _ in range(args.warmup):
+        cpu_decode_step(sub)
+    t = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_decode_step(sub)
+        t.append(time.perf_counter() - t0)
+    mean = float(np.mean(t))
+    value = sub["bytes"] / mean / 1e9
+    cores = _blas_threads()
+    sample = (f"{len(seqs)} of 256 config-2 sequences per step (store + decode, fp32 numpy restatement of "
+              f"qwen3.py:240-264 + 430-542)")
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(mean * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (bf16-valued inputs)",
+        "data": "synthetic",
+        "config": {"workload": "config2: decode paged attention + 1-token store_kvcache per sequence (sampled)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

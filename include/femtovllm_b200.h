@@ -1,0 +1,134 @@
+/*
+ * femtovllm_b200.h - C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Drop-in replacement for the native entry points of fishAndShrimp/
+ * nano-vllm-practice ("FemtoVLLM") on its attention path.  All functions take
+ * plain device pointers, sizes and a CUDA stream (as void*), never allocate,
+ * and return an fvb_status.  Tensor layouts are the reference's:
+ *
+ *   K/V pool    [num_blocks][n_kv_heads][block_size = 16][head_dim], contiguous
+ *               (femtovllm/engine/core_engine.py:140-162)
+ *   q, out      [n_heads][q_len_flatten][head_dim], contiguous ("head-major",
+ *               femtovllm/ops/__init__.py:82-156)
+ *   block table int32 [num_seqs][max_blocks_per_seq], -1 padded
+ *               (femtovllm/engine/model_runner.py:46-72)
+ *   kv_lens, positions, cu_seqlens: int32
+ *
+ * dtype codes: FVB_DTYPE_F32, FVB_DTYPE_BF16, FVB_DTYPE_F16.
+ * head_dim: 64 or 128.  n_heads / n_kv_heads (GQA group): 1, 2, 4 or 8.
+ */
+#ifndef FEMTOVLLM_B200_H_
+#define FEMTOVLLM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FVB_API __attribute__((visibility("default")))
+#else
+#define FVB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FVB_DTYPE_F32 = 0,
+  FVB_DTYPE_BF16 = 1,
+  FVB_DTYPE_F16 = 2,
+};
+
+typedef enum fvb_status {
+  FVB_OK = 0,
+  FVB_ERR_INVALID_ARGUMENT = 1,   /* null pointer, negative size, inconsistent shapes */
+  FVB_ERR_UNSUPPORTED = 2,        /* dtype / head_dim / GQA group / block_size not built */
+  FVB_ERR_MISALIGNED = 3,         /* a pointer or stride breaks the 16-byte rule */
+  FVB_ERR_WORKSPACE_TOO_SMALL = 4,
+  FVB_ERR_CUDA = 5,               /* a CUDA runtime call failed (see fvb_last_cuda_error) */
+  FVB_ERR_DEVICE_TIMEOUT = 6,     /* a bounded device-side wait gave up */
+  FVB_ERR_BAD_PAGE = 7,           /* block-table entry < 0 or >= num_blocks inside kv_len */
+  FVB_ERR_BAD_SLOT = 8,           /* slot_mapping entry >= num_blocks * block_size */
+  FVB_ERR_NO_DEVICE_SUPPORT = 9,  /* the current device is not sm_100 */
+} fvb_status;
+
+/* Human-readable name of a status code (static storage). */
+FVB_API const char* fvb_status_string(int status);
+
+/* Last CUDA runtime error code seen by an entry point on this thread (0 if none). */
+FVB_API int fvb_last_cuda_error(void);
+
+/* Compile-time contract constants, exported like femtovllm._C's attributes
+ * (csrc/bindings.cpp:62-66: kKVLenPerPage, kDimHead, kMaxKVLenNonSplit).
+ * fvb_max_kv_len() replaces kMaxKVLenNonSplit = 8192
+ * (csrc/utils/constants.cuh:39): decode here is split-KV, so the only limit is
+ * the int32 indexing of the block table. */
+FVB_API int fvb_kv_len_per_page(void);
+FVB_API int fvb_dim_head(void);
+FVB_API int fvb_max_kv_len(void);
+
+/* Read and clear the device error word that kernels set when they meet a bad
+ * page or slot, or give up a bounded wait.  Synchronizes `stream`.
+ * *code = 0 when nothing was recorded; *info is the first failing index/site. */
+FVB_API int fvb_read_device_error(int* code, int* info, void* stream);
+
+/*
+ * store_kvcache: pool[slot / 16][h][slot % 16][:] = new[t][h][:] for K and V.
+ *
+ * Replaces the Python KV-write loops of QwenSelfAttention
+ * (femtovllm/models/qwen/qwen3.py:240-264 decode, 322-366 prefill,
+ * 450-490 PyTorch path), which have no native counterpart in the reference.
+ * slot_mapping[t] = block_table[s][pos_t / 16] * 16 + pos_t % 16, int64;
+ * -1 skips the token.  k / v: [num_tokens][n_kv_heads][head_dim] with
+ * element strides (token_stride, head_stride, 1).  Bit-exact copy.
+ */
+FVB_API int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride,
+                      void* k_pool, void* v_pool, int64_t num_blocks, const int64_t* slot_mapping,
+                      int64_t num_tokens, int n_kv_heads, int head_dim, int block_size, int dtype,
+                      void* stream);
+
+/*
+ * Decode paged attention (one query token per sequence), split-KV.
+ *
+ * Replaces PagedAttentionGemvCuda (csrc/paged_attention/paged_attention_gemv.cu:223-308,
+ * bound at csrc/bindings.cpp:52-59; Python wrapper femtovllm/ops/__init__.py:82-107).
+ * q, out: [n_heads][num_seqs][head_dim]; out[h][b] = softmax(q k^T / sqrt(D)) v over
+ * keys 0 .. kv_lens[b]-1 of kv head h / (n_heads / n_kv_heads).
+ * max_kv_len must be >= every kv_lens[b] (the reference passes it from the host).
+ * workspace: device buffer of at least fvb_paged_attention_decode_workspace_size() bytes.
+ */
+FVB_API size_t fvb_paged_attention_decode_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
+                                                 int max_kv_len);
+FVB_API int fvb_paged_attention_decode(const void* q, void* out, const void* k_pool, const void* v_pool,
+                               int64_t num_blocks, int n_heads, int n_kv_heads, int head_dim, int block_size,
+                               int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
+                               const int32_t* kv_lens, int max_kv_len, int dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
+ * Varlen chunked-prefill causal attention over paged, prefix-cached KV.
+ *
+ * Replaces PagedAttentionGemmCuda (csrc/paged_attention/paged_attention_gemm.cu:304-394,
+ * bound at csrc/bindings.cpp:41-50) and the default Triton prefill
+ * paged_attention_gemm_triton (femtovllm/ops/triton/paged_attention/paged_attention_gemm.py:165-235);
+ * Python wrapper femtovllm/ops/__init__.py:110-156.
+ * q, out: [n_heads][q_len_flatten][head_dim]; sequence s owns query tokens
+ * cu_seqlens[s] .. cu_seqlens[s+1]-1; query i sees key j iff j < kv_lens[s] and
+ * j <= positions[i].  Sequences with one new token (decode rows) may be mixed in
+ * the same launch (the reference's unified CUSTOM_GEMM route, qwen3.py:575-581).
+ * bf16 / f16 run on tcgen05 tensor cores; f32 runs on a SIMT fp32 kernel.
+ */
+FVB_API size_t fvb_paged_attention_prefill_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
+                                                  int64_t q_len_flatten, int max_q_len);
+FVB_API int fvb_paged_attention_prefill(const void* q, void* out, const void* k_pool, const void* v_pool,
+                                int64_t num_blocks, int n_heads, int n_kv_heads, int head_dim, int block_size,
+                                int num_seqs, int64_t q_len_flatten, const int32_t* cu_seqlens, int max_q_len,
+                                const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
+                                const int32_t* positions, int dtype, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FEMTOVLLM_B200_H_ */

@@ -1,0 +1,247 @@
+// extern "C" entry points of libfemtovllm_b200.so (declared in
+// include/femtovllm_b200.h).  Host-side validation of every scalar argument,
+// the 16-byte alignment rules of the TMA / vector paths, workspace sizing,
+// and mapping of CUDA errors to fvb_status.  Nothing here allocates.
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fvb {
+
+// {first error code, its info} since the last fvb_read_device_error on this device.
+__device__ int g_device_error[2] = {0, 0};
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+int* g_err_ptr[kMaxDevices] = {};
+
+// Device address of g_device_error on the current device (resolved once per device).
+int* device_error_ptr(cudaError_t* e) {
+  int dev = 0;
+  *e = cudaGetDevice(&dev);
+  if (*e != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= kMaxDevices) {
+    *e = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  if (!g_err_ptr[dev]) {
+    void* p = nullptr;
+    *e = cudaGetSymbolAddress(&p, g_device_error);
+    if (*e != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_err_ptr[dev];
+}
+
+thread_local int t_last_cuda_error = 0;
+
+int esize_of(int dtype) {
+  switch (dtype) {
+    case FVB_DTYPE_F32:
+      return 4;
+    case FVB_DTYPE_BF16:
+    case FVB_DTYPE_F16:
+      return 2;
+    default:
+      return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return FVB_OK;
+  t_last_cuda_error = int(e);
+  return FVB_ERR_CUDA;
+}
+
+bool gqa_ok(int n_heads, int n_kv_heads) {
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads) return false;
+  const int r = n_heads / n_kv_heads;
+  return r == 1 || r == 2 || r == 4 || r == 8;
+}
+
+// Common checks of the attention entry points.
+int check_attention(const void* q, const void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                    int n_heads, int n_kv_heads, int head_dim, int block_size, int num_seqs,
+                    const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens, int dtype) {
+  if (esize_of(dtype) == 0) return FVB_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return FVB_ERR_UNSUPPORTED;
+  if (block_size != kPageSize) return FVB_ERR_UNSUPPORTED;
+  if (!gqa_ok(n_heads, n_kv_heads)) return FVB_ERR_UNSUPPORTED;
+  if (num_seqs < 0 || num_blocks < 1 || max_blocks_per_seq < 0) return FVB_ERR_INVALID_ARGUMENT;
+  if (num_seqs > 0 && (!q || !out || !k_pool || !v_pool || !block_tables || !kv_lens))
+    return FVB_ERR_INVALID_ARGUMENT;
+  if (num_blocks * n_kv_heads * kPageSize > int64_t(0x7fffffff)) return FVB_ERR_UNSUPPORTED;  // TMA row coordinate
+  if (!aligned16(q) || !aligned16(out) || !aligned16(k_pool) || !aligned16(v_pool)) return FVB_ERR_MISALIGNED;
+  return FVB_OK;
+}
+
+}  // namespace
+
+int device_sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+cudaError_t make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
+                        uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+  static EncodeTiledFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &qres);
+    if (e != cudaSuccess) return e;
+    if (qres != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace fvb
+
+using namespace fvb;
+
+extern "C" {
+
+const char* fvb_status_string(int status) {
+  switch (status) {
+    case FVB_OK:
+      return "FVB_OK";
+    case FVB_ERR_INVALID_ARGUMENT:
+      return "FVB_ERR_INVALID_ARGUMENT";
+    case FVB_ERR_UNSUPPORTED:
+      return "FVB_ERR_UNSUPPORTED";
+    case FVB_ERR_MISALIGNED:
+      return "FVB_ERR_MISALIGNED";
+    case FVB_ERR_WORKSPACE_TOO_SMALL:
+      return "FVB_ERR_WORKSPACE_TOO_SMALL";
+    case FVB_ERR_CUDA:
+      return "FVB_ERR_CUDA";
+    case FVB_ERR_DEVICE_TIMEOUT:
+      return "FVB_ERR_DEVICE_TIMEOUT";
+    case FVB_ERR_BAD_PAGE:
+      return "FVB_ERR_BAD_PAGE";
+    case FVB_ERR_BAD_SLOT:
+      return "FVB_ERR_BAD_SLOT";
+    case FVB_ERR_NO_DEVICE_SUPPORT:
+      return "FVB_ERR_NO_DEVICE_SUPPORT";
+    default:
+      return "FVB_ERR_UNKNOWN";
+  }
+}
+
+int fvb_last_cuda_error(void) { return t_last_cuda_error; }
+
+int fvb_kv_len_per_page(void) { return kPageSize; }
+int fvb_dim_head(void) { return 128; }
+int fvb_max_kv_len(void) { return 1 << 30; }
+
+int fvb_read_device_error(int* code, int* info, void* stream) {
+  if (!code || !info) return FVB_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = cuda_status(cudaStreamSynchronize(s));
+  if (st) return st;
+  int word[2] = {0, 0};
+  st = cuda_status(cudaMemcpyFromSymbol(word, g_device_error, sizeof(word)));
+  if (st) return st;
+  *code = word[0];
+  *info = word[1];
+  const int zero[2] = {0, 0};
+  return cuda_status(cudaMemcpyToSymbol(g_device_error, zero, sizeof(zero)));
+}
+
+int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride, void* k_pool,
+                      void* v_pool, int64_t num_blocks, const int64_t* slot_mapping, int64_t num_tokens,
+                      int n_kv_heads, int head_dim, int block_size, int dtype, void* stream) {
+  const int es = esize_of(dtype);
+  if (es == 0) return FVB_ERR_UNSUPPORTED;
+  if (num_tokens < 0 || n_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || num_blocks < 0 ||
+      token_stride < 0 || head_stride < 0)
+    return FVB_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return FVB_OK;
+  if (!k || !v || !k_pool || !v_pool || !slot_mapping) return FVB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(slot_mapping) & 7) != 0) return FVB_ERR_MISALIGNED;
+  cudaError_t e;
+  int* err = device_error_ptr(&e);
+  if (!err) return cuda_status(e);
+  return cuda_status(launch_store_kvcache(k, v, token_stride, head_stride, k_pool, v_pool, num_blocks, slot_mapping,
+                                          num_tokens, n_kv_heads, head_dim, block_size, es, err,
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+size_t fvb_paged_attention_decode_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
+                                                 int max_kv_len) {
+  if (num_seqs <= 0 || !gqa_ok(n_heads, n_kv_heads)) return 0;
+  return plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count()).ws_bytes;
+}
+
+int fvb_paged_attention_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                               int n_heads, int n_kv_heads, int head_dim, int block_size, int num_seqs,
+                               const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
+                               int max_kv_len, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_attention(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
+                           block_tables, max_blocks_per_seq, kv_lens, dtype);
+  if (st) return st;
+  if (num_seqs == 0) return FVB_OK;
+  if (max_kv_len < 0 || int64_t(max_kv_len) > int64_t(max_blocks_per_seq) * kPageSize) return FVB_ERR_INVALID_ARGUMENT;
+  const DecodePlan plan = plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count());
+  if (plan.ws_bytes > 0 && (!workspace || workspace_bytes < plan.ws_bytes)) return FVB_ERR_WORKSPACE_TOO_SMALL;
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255)) return FVB_ERR_MISALIGNED;
+  cudaError_t e;
+  int* err = device_error_ptr(&e);
+  if (!err) return cuda_status(e);
+  return cuda_status(launch_decode(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
+                                   block_tables, max_blocks_per_seq, kv_lens, max_kv_len, dtype, plan, workspace, err,
+                                   static_cast<cudaStream_t>(stream)));
+}
+
+size_t fvb_paged_attention_prefill_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
+                                                  int64_t q_len_flatten, int max_q_len) {
+  (void)num_seqs;
+  (void)n_heads;
+  (void)n_kv_heads;
+  (void)head_dim;
+  (void)q_len_flatten;
+  (void)max_q_len;
+  return 0;
+}
+
+int fvb_paged_attention_prefill(const void* q, void* out, const void* k_pool, const void* v_pool,
+                                int64_t num_blocks, int n_heads, int n_kv_heads, int head_dim, int block_size,
+                                int num_seqs, int64_t q_len_flatten, const int32_t* cu_seqlens, int max_q_len,
+                                const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
+                                const int32_t* positions, int dtype, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  int st = check_attention(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
+                           block_tables, max_blocks_per_seq, kv_lens, dtype);
+  if (st) return st;
+  if (q_len_flatten < 0 || max_q_len < 0) return FVB_ERR_INVALID_ARGUMENT;
+  if (num_seqs == 0 || q_len_flatten == 0) return FVB_OK;
+  if (!cu_seqlens || !positions) return FVB_ERR_INVALID_ARGUMENT;
+  cudaError_t e;
+  int* err = device_error_ptr(&e);
+  if (!err) return cuda_status(e);
+  return cuda_status(launch_prefill_simt(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
+                                         q_len_flatten, cu_seqlens, block_tables, max_blocks_per_seq, kv_lens,
+                                         positions, dtype, err, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,478 @@
+// Decode paged attention over block tables with GQA: split-KV ("flash
+// decoding") on SIMT cores, HBM-bound.
+//
+// Replaces PagedAttentionGemvKernel (csrc/paged_attention/paged_attention_gemv.cu:16-221
+// of the reference), which runs one CTA per (sequence, query head), re-reads
+// every K/V page once per query head of a GQA group with 2-byte strided loads,
+// and keeps all scores in shared memory (so kv_len <= 8192).
+//
+// Here one CTA serves one (KV split, kv head, sequence) and all n_rep query
+// heads of the group, so each K/V byte leaves HBM once:
+//
+//   warp 0      producer: lane 0 walks the split's pages through the block
+//               table and streams them into a 4-slot shared-memory ring, K
+//               pages by 2-D TMA with 128-byte swizzle, V pages by 1-D bulk
+//               copy; completion is signalled on per-slot mbarriers.
+//   warps 1..4  consumers: warp w owns ring slot w (stages w, w+4, ...).  A
+//               stage is 32 tokens (2 pages); lane t computes the full q.k dot
+//               products of token t for all n_rep heads (q broadcast from
+//               shared memory, K chunks read through the swizzle so the 32
+//               lanes hit distinct banks), the warp keeps an online softmax in
+//               the log2 domain, then lane l accumulates p * V for head dims
+//               [l*D/32, (l+1)*D/32) over the stage's tokens.
+//
+// At the end the four warps' (max, sum, acc) are merged in shared memory; a
+// sequence with a single split writes its output directly, otherwise the
+// normalised partial and its log-sum-exp go to the workspace and
+// decode_combine_kernel merges the splits.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fvb {
+namespace {
+
+constexpr int kStageTokens = 32;  // one token per lane
+constexpr int kStagePages = kStageTokens / kPageSize;
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeThreads = 32 * (1 + kConsumerWarps);
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <typename T, int D, int NREP>
+struct DecodeTraits {
+  static constexpr int kEsize = sizeof(T);
+  static constexpr int kRowBytes = D * kEsize;     // one token of one kv head: 128, 256 or 512 B
+  static constexpr int kHalves = kRowBytes / 128;  // 128-byte TMA boxes per row
+  static constexpr int kBoxCols = 128 / kEsize;
+  static constexpr int kPageBytes = kPageSize * kRowBytes;
+  static constexpr int kStageBytes = kStageTokens * kRowBytes;  // K (or V) bytes of one stage
+  static constexpr int kChunks = kRowBytes / 16;                // 16-byte chunks per K row
+  static constexpr int kVec = 16 / kEsize;                      // elements per chunk
+  static constexpr int kDPL = D / 32;                           // V dims per lane
+  static constexpr int kSlots = kConsumerWarps;
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kSlots * kStageBytes;
+  static constexpr int kOffQ = 2 * kSlots * kStageBytes;      // float [NREP][D], pre-scaled to log2 units
+  static constexpr int kOffP = kOffQ + NREP * D * 4;          // float [warp][token][NREP]
+  static constexpr int kOffBar = kOffP + kConsumerWarps * kStageTokens * NREP * 4;
+  static constexpr int kSmemBytes = kOffBar + 2 * kSlots * 8 + 1024;  // + 1024-B alignment slack
+  // Warp-merge scratch (float acc[warp][NREP][D], m[warp][NREP], l[warp][NREP]) aliases the ring.
+  static_assert(kConsumerWarps * NREP * (D + 2) * 4 <= 2 * kSlots * kStageBytes, "merge scratch");
+  static_assert(kRowBytes % 128 == 0, "row must be whole 128-byte swizzle spans");
+};
+
+template <typename T, int DPL>
+__device__ __forceinline__ void load_dims(uint32_t addr, float* f) {
+  constexpr int kBytes = DPL * sizeof(T);
+  if constexpr (kBytes == 16) {
+    unpack16<T>(lds_v4(addr), f);
+  } else if constexpr (kBytes == 8) {
+    uint32_t a, b;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
+    if constexpr (sizeof(T) == 4) {
+      f[0] = __uint_as_float(a);
+      f[1] = __uint_as_float(b);
+    } else {
+      uint4 v = make_uint4(a, b, 0, 0);
+      float tmp[8];
+      unpack16<T>(v, tmp);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) f[i] = tmp[i];
+    }
+  } else {
+    static_assert(kBytes == 4, "dims per lane");
+    uint32_t a;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a) : "r"(addr));
+    uint4 v = make_uint4(a, 0, 0, 0);
+    float tmp[8];
+    unpack16<T>(v, tmp);
+    f[0] = tmp[0];
+    f[1] = tmp[1];
+  }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T, int D, int NREP>
+__global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
+    const __grid_constant__ CUtensorMap kmap, const T* __restrict__ q, T* __restrict__ out,
+    const uint8_t* __restrict__ v_pool, int64_t num_blocks, int n_kv_heads, int num_seqs,
+    const int32_t* __restrict__ block_tables, int max_blocks_per_seq, const int32_t* __restrict__ kv_lens,
+    int kv_cap, int pages_per_split, int max_splits, float* __restrict__ ws_o, float* __restrict__ ws_lse,
+    int* __restrict__ err) {
+  using Tr = DecodeTraits<T, D, NREP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* qs = reinterpret_cast<float*>(smem + Tr::kOffQ);
+  float* ps = reinterpret_cast<float*>(smem + Tr::kOffP);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Tr::kOffBar);
+  uint64_t* empty = full + Tr::kSlots;
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_heads = n_kv_heads * NREP;
+  int kv_len = max(__ldg(kv_lens + b), 0);
+  if (kv_len > kv_cap) {
+    // Longer than max_kv_len or than the block table row: never read past either.
+    if (split == 0 && threadIdx.x == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, b);
+    kv_len = kv_cap;
+  }
+  const int npages = (kv_len + kPageSize - 1) / kPageSize;
+  const int nsplits = (npages + pages_per_split - 1) / pages_per_split;
+  const int page_begin = split * pages_per_split;
+
+  if (npages == 0) {
+    // Empty context: the reference never produces one; emit zeros, not garbage.
+    if (split == 0) {
+      for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
+        const int r = e / D, d = e % D;
+        out[(int64_t(kvh * NREP + r) * num_seqs + b) * D + d] = Elem<T>::from_f(0.f);
+      }
+    }
+    return;
+  }
+  if (page_begin >= npages) return;  // this split lies past the sequence (uniform per CTA)
+  const int page_end = min(npages, page_begin + pages_per_split);
+  const int n_iter = (page_end - page_begin + kStagePages - 1) / kStagePages;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Tr::kSlots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  // q for the NREP heads of this group, fp32, scaled so scores are in log2 units.
+  {
+    const float scale = kLog2e * rsqrtf(float(D));
+    for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
+      const int r = e / D, d = e % D;
+      qs[e] = Elem<T>::to_f(q[(int64_t(kvh * NREP + r) * num_seqs + b) * D + d]) * scale;
+    }
+  }
+  __syncthreads();
+
+  const int32_t* table = block_tables + int64_t(b) * max_blocks_per_seq;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&kmap);
+      for (int it = 0; it < n_iter; ++it) {
+        const int slot = it % Tr::kSlots;
+        const int use = it / Tr::kSlots;
+        if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1, err, 0x100 + slot)) return;
+        const int p0 = page_begin + it * kStagePages;
+        const int np = min(kStagePages, page_end - p0);
+        mbar_arrive_expect_tx(&full[slot], uint32_t(np) * 2u * Tr::kPageBytes);
+        uint8_t* kdst = smem + Tr::kOffK + slot * Tr::kStageBytes;
+        uint8_t* vdst = smem + Tr::kOffV + slot * Tr::kStageBytes;
+        for (int j = 0; j < np; ++j) {
+          int blk = __ldg(table + p0 + j);
+          if (blk < 0 || blk >= num_blocks) {
+            record_error(err, FVB_ERR_BAD_PAGE, b);
+            blk = 0;  // keep the copy in bounds; the error word reports the bad table
+          }
+          const int row = (blk * n_kv_heads + kvh) * kPageSize;
+#pragma unroll
+          for (int hf = 0; hf < Tr::kHalves; ++hf) {
+            tma_load_2d(kdst + j * Tr::kPageBytes + hf * 2048, &kmap, hf * Tr::kBoxCols, row, &full[slot]);
+          }
+          bulk_g2s(vdst + j * Tr::kPageBytes, v_pool + int64_t(row) * Tr::kRowBytes, Tr::kPageBytes, &full[slot]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int cw = warp - 1;
+  float m[NREP], l[NREP], acc[NREP][Tr::kDPL];
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < Tr::kDPL; ++i) acc[r][i] = 0.f;
+  }
+  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t qs_addr = smem_u32(qs);
+  float* pw = ps + cw * kStageTokens * NREP;
+  const uint32_t pw_addr = smem_u32(pw);
+  // Lane-constant part of this lane's K row address inside a slot.
+  const int kr = lane & 15;
+  const uint32_t k_lane_off = (lane >> 4) * Tr::kPageBytes + kr * 128;
+  bool ok = true;
+
+  for (int it = cw; it < n_iter; it += kConsumerWarps) {
+    const int slot = it % Tr::kSlots;
+    if (!mbar_wait(&full[slot], (it / Tr::kSlots) & 1, err, 0x200 + slot)) {
+      ok = false;
+      break;
+    }
+    const int tok0 = (page_begin + it * kStagePages) * kPageSize;
+    const int nvalid = min(kStageTokens, kv_len - tok0);
+    const uint32_t kslot = smem_base + Tr::kOffK + slot * Tr::kStageBytes;
+    const uint32_t vslot = smem_base + Tr::kOffV + slot * Tr::kStageBytes;
+
+    // s[r] = q_r . k_lane  (log2 units)
+    float s[NREP];
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) s[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < Tr::kChunks; ++c) {
+      const uint32_t kaddr = kslot + k_lane_off + (c >> 3) * 2048 + ((((c & 7) ^ (kr & 7))) << 4);
+      float kf[Tr::kVec];
+      unpack16<T>(lds_v4(kaddr), kf);
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) {
+#pragma unroll
+        for (int e = 0; e < Tr::kVec; e += 4) {
+          const float4 qv = *reinterpret_cast<const float4*>(qs + r * D + c * Tr::kVec + e);
+          s[r] = fmaf(qv.x, kf[e + 0], s[r]);
+          s[r] = fmaf(qv.y, kf[e + 1], s[r]);
+          s[r] = fmaf(qv.z, kf[e + 2], s[r]);
+          s[r] = fmaf(qv.w, kf[e + 3], s[r]);
+        }
+      }
+    }
+    const bool valid = lane < nvalid;
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      const float sr = valid ? s[r] : -INFINITY;
+      const float mn = fmaxf(m[r], warp_max(sr));  // finite: token 0 of a stage is always valid
+      const float corr = fast_exp2(m[r] - mn);
+      const float p = fast_exp2(sr - mn);
+      m[r] = mn;
+      l[r] = l[r] * corr + p;
+#pragma unroll
+      for (int i = 0; i < Tr::kDPL; ++i) acc[r][i] *= corr;
+      pw[lane * NREP + r] = p;
+    }
+    __syncwarp();
+    // acc[r][:] += sum_t p[t][r] * V[t][lane dims]
+    const uint32_t v_lane = vslot + lane * Tr::kDPL * Tr::kEsize;
+#pragma unroll 4
+    for (int t = 0; t < nvalid; ++t) {
+      float vf[Tr::kDPL];
+      load_dims<T, Tr::kDPL>(v_lane + t * Tr::kRowBytes, vf);
+      float pr[NREP];
+      if constexpr (NREP % 4 == 0) {
+#pragma unroll
+        for (int r = 0; r < NREP; r += 4) {
+          const float4 pv = *reinterpret_cast<const float4*>(pw + t * NREP + r);
+          pr[r] = pv.x;
+          pr[r + 1] = pv.y;
+          pr[r + 2] = pv.z;
+          pr[r + 3] = pv.w;
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < NREP; ++r) pr[r] = pw[t * NREP + r];
+      }
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) {
+#pragma unroll
+        for (int i = 0; i < Tr::kDPL; ++i) acc[r][i] = fmaf(pr[r], vf[i], acc[r][i]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  (void)pw_addr;
+  (void)qs_addr;
+
+  // ---------------- merge the four warps ----------------
+  named_barrier(1, 32 * kConsumerWarps);  // every consumer is done with the ring
+  float* wacc = reinterpret_cast<float*>(smem);                 // [warp][NREP][D]
+  float* wm = wacc + kConsumerWarps * NREP * D;                 // [warp][NREP]
+  float* wl = wm + kConsumerWarps * NREP;                       // [warp][NREP]
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    const float lsum = warp_sum(l[r]);
+    if (lane == 0) {
+      wm[cw * NREP + r] = ok ? m[r] : -INFINITY;
+      wl[cw * NREP + r] = ok ? lsum : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < Tr::kDPL; ++i) wacc[(cw * NREP + r) * D + lane * Tr::kDPL + i] = ok ? acc[r][i] : 0.f;
+  }
+  named_barrier(1, 32 * kConsumerWarps);
+  const int tid = threadIdx.x - 32;
+  for (int e = tid; e < NREP * D; e += 32 * kConsumerWarps) {
+    const int r = e / D, d = e % D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, wm[w * NREP + r]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float f = fast_exp2(wm[w * NREP + r] - mx);
+      L += wl[w * NREP + r] * f;
+      O += wacc[(w * NREP + r) * D + d] * f;
+    }
+    const int head = kvh * NREP + r;
+    if (nsplits == 1) {
+      out[(int64_t(head) * num_seqs + b) * D + d] = Elem<T>::from_f(O / L);
+    } else {
+      const int64_t idx = (int64_t(b) * n_heads + head) * max_splits + split;
+      ws_o[idx * D + d] = O / L;
+      if (d == 0) ws_lse[idx] = mx + __log2f(L);
+    }
+  }
+}
+
+// Merge the split partials of every (sequence, head) that has more than one
+// split.  One warp per (sequence, head); lane l owns dims [l*D/32, (l+1)*D/32).
+template <typename T, int D>
+__global__ void __launch_bounds__(256) decode_combine_kernel(const float* __restrict__ ws_o,
+                                                             const float* __restrict__ ws_lse, T* __restrict__ out,
+                                                             const int32_t* __restrict__ kv_lens, int kv_cap,
+                                                             int num_seqs, int n_heads, int pages_per_split,
+                                                             int max_splits) {
+  constexpr int kDPL = D / 32;
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (gw >= num_seqs * n_heads) return;
+  const int b = gw / n_heads, head = gw % n_heads;
+  const int kv_len = min(max(__ldg(kv_lens + b), 0), kv_cap);
+  const int npages = (kv_len + kPageSize - 1) / kPageSize;
+  const int nsplits = (npages + pages_per_split - 1) / pages_per_split;
+  if (nsplits <= 1) return;
+  const int64_t base = (int64_t(b) * n_heads + head) * max_splits;
+  float mx = -INFINITY;
+  for (int s = lane; s < nsplits; s += 32) mx = fmaxf(mx, ws_lse[base + s]);
+  mx = warp_max(mx);
+  float L = 0.f, o[kDPL];
+#pragma unroll
+  for (int i = 0; i < kDPL; ++i) o[i] = 0.f;
+  for (int s = 0; s < nsplits; ++s) {
+    const float w = fast_exp2(__ldg(ws_lse + base + s) - mx);
+    L += w;
+    const float* src = ws_o + (base + s) * D + lane * kDPL;
+#pragma unroll
+    for (int i = 0; i < kDPL; ++i) o[i] = fmaf(w, __ldg(src + i), o[i]);
+  }
+  const float inv = 1.f / L;
+#pragma unroll
+  for (int i = 0; i < kDPL; ++i) {
+    out[(int64_t(head) * num_seqs + b) * D + lane * kDPL + i] = Elem<T>::from_f(o[i] * inv);
+  }
+}
+
+template <typename T, int D, int NREP>
+cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                            int n_kv_heads, int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
+                            const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan, void* workspace,
+                            int* err, cudaStream_t stream) {
+  using Tr = DecodeTraits<T, D, NREP>;
+  const int kv_cap = int(std::min<int64_t>(std::min<int64_t>(max_kv_len, int64_t(max_blocks_per_seq) * kPageSize),
+                                           int64_t(plan.max_splits) * plan.pages_per_split * kPageSize));
+  CUtensorMap kmap;
+  const CUtensorMapDataType tdt = sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cudaError_t ce = make_tma_2d(&kmap, k_pool, tdt, D, uint64_t(num_blocks) * n_kv_heads * kPageSize,
+                                Tr::kRowBytes, Tr::kBoxCols, kPageSize, true);
+  if (ce != cudaSuccess) return ce;
+  auto kern = decode_split_kernel<T, D, NREP>;
+  ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  if (ce != cudaSuccess) return ce;
+  float* ws_o = nullptr;
+  float* ws_lse = nullptr;
+  if (plan.max_splits > 1) {
+    ws_o = static_cast<float*>(workspace);
+    const size_t o_bytes = size_t(num_seqs) * n_kv_heads * NREP * plan.max_splits * D * 4;
+    ws_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((o_bytes + 255) & ~size_t(255)));
+  }
+  dim3 grid(plan.max_splits, n_kv_heads, num_seqs);
+  kern<<<grid, kDecodeThreads, Tr::kSmemBytes, stream>>>(
+      kmap, static_cast<const T*>(q), static_cast<T*>(out), static_cast<const uint8_t*>(v_pool), num_blocks,
+      n_kv_heads, num_seqs, block_tables, max_blocks_per_seq, kv_lens, kv_cap, plan.pages_per_split, plan.max_splits,
+      ws_o, ws_lse, err);
+  ce = cudaGetLastError();
+  if (ce != cudaSuccess || plan.max_splits <= 1) return ce;
+  const int warps = num_seqs * n_kv_heads * NREP;
+  decode_combine_kernel<T, D><<<(warps + 7) / 8, 256, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), kv_lens,
+                                                                   kv_cap, num_seqs, n_kv_heads * NREP,
+                                                                   plan.pages_per_split, plan.max_splits);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t dispatch_nrep(int nrep, const void* q, void* out, const void* k_pool, const void* v_pool,
+                          int64_t num_blocks, int n_kv_heads, int num_seqs, const int32_t* block_tables,
+                          int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan,
+                          void* ws, int* err, cudaStream_t stream) {
+  switch (nrep) {
+    case 1:
+      return launch_decode_t<T, D, 1>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+    case 2:
+      return launch_decode_t<T, D, 2>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+    case 4:
+      return launch_decode_t<T, D, 4>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+    case 8:
+      return launch_decode_t<T, D, 8>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+DecodePlan plan_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int max_kv_len, int num_sms) {
+  DecodePlan p{};
+  const int max_pages = std::max(1, (max_kv_len + kPageSize - 1) / kPageSize);
+  const int64_t units = int64_t(num_seqs) * n_kv_heads;
+  // Enough CTAs for ~4 waves of 3 resident CTAs per SM, but no split shorter
+  // than 4 pages (64 tokens) and none longer than 64 pages (1024 tokens), so
+  // the last wave's tail stays short for long contexts.
+  const int64_t target = int64_t(num_sms) * 3 * 4;
+  int pps = 64;
+  while (pps > 4 && units * ((max_pages + pps - 1) / pps) < target) pps /= 2;
+  p.pages_per_split = pps;
+  p.max_splits = (max_pages + pps - 1) / pps;
+  if (p.max_splits > 1) {
+    const size_t o_bytes = size_t(num_seqs) * n_heads * p.max_splits * head_dim * 4;
+    const size_t lse_bytes = size_t(num_seqs) * n_heads * p.max_splits * 4;
+    p.ws_bytes = ((o_bytes + 255) & ~size_t(255)) + lse_bytes;
+  } else {
+    p.ws_bytes = 0;
+  }
+  return p;
+}
+
+cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                          int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
+                          int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
+                          const DecodePlan& plan, void* workspace, int* err, cudaStream_t stream) {
+  if (num_seqs == 0) return cudaSuccess;
+  const int nrep = n_heads / n_kv_heads;
+#define FVB_DECODE_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables, \
+                        max_blocks_per_seq, kv_lens, max_kv_len, plan, workspace, err, stream
+  if (dtype == FVB_DTYPE_BF16) {
+    return head_dim == 128 ? dispatch_nrep<__nv_bfloat16, 128>(FVB_DECODE_ARGS)
+                           : dispatch_nrep<__nv_bfloat16, 64>(FVB_DECODE_ARGS);
+  } else if (dtype == FVB_DTYPE_F16) {
+    return head_dim == 128 ? dispatch_nrep<__half, 128>(FVB_DECODE_ARGS) : dispatch_nrep<__half, 64>(FVB_DECODE_ARGS);
+  } else {
+    return head_dim == 128 ? dispatch_nrep<float, 128>(FVB_DECODE_ARGS) : dispatch_nrep<float, 64>(FVB_DECODE_ARGS);
+  }
+#undef FVB_DECODE_ARGS
+}
+
+}  // namespace fvb

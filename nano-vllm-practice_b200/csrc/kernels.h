@@ -1,0 +1,59 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace fvb {
+
+// Host-side encoder for 2-D tiled TMA descriptors (cuTensorMapEncodeTiled,
+// resolved through the runtime's driver entry point so nothing links libcuda).
+// rows x cols elements, row pitch `row_bytes`, box {box_cols, box_rows},
+// 128-byte swizzle when swizzle128 is set.
+cudaError_t make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols,
+                        uint64_t rows, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128);
+
+cudaError_t launch_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride,
+                                 void* k_pool, void* v_pool, int64_t num_blocks, const int64_t* slot_mapping,
+                                 int64_t num_tokens, int n_kv_heads, int head_dim, int block_size, int esize,
+                                 int* err, cudaStream_t stream);
+
+// Split-KV plan of one decode launch.  Deterministic in its inputs and the
+// device's SM count, so the workspace size can be asked for ahead of the call.
+struct DecodePlan {
+  int pages_per_split;  // multiple of the 2-page stage
+  int max_splits;       // ceil(ceil(max_kv_len / 16) / pages_per_split)
+  size_t ws_bytes;      // partial outputs + log-sum-exps
+};
+DecodePlan plan_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int max_kv_len, int num_sms);
+
+cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                          int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
+                          int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
+                          const DecodePlan& plan, void* workspace, int* err, cudaStream_t stream);
+
+struct PrefillPlan {
+  int tile_tokens;      // query tokens per tile (128 / GQA group on the tensor-core path)
+  int64_t max_tiles;    // upper bound on query tiles over all sequences
+  size_t ws_bytes;
+};
+PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int64_t q_len_flatten,
+                         int max_q_len, int dtype);
+
+cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                           int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,
+                           const int32_t* cu_seqlens, int max_q_len, const int32_t* block_tables,
+                           int max_blocks_per_seq, const int32_t* kv_lens, const int32_t* positions, int dtype,
+                           const PrefillPlan& plan, void* workspace, int* err, cudaStream_t stream);
+
+cudaError_t launch_prefill_simt(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,
+                                const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
+                                const int32_t* kv_lens, const int32_t* positions, int dtype, int* err,
+                                cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace fvb

@@ -1,0 +1,183 @@
+// femtovllm_b200._C: the PyTorch face of libfemtovllm_b200.so.
+//
+// Mirrors the reference's native module femtovllm._C (csrc/bindings.cpp:41-66):
+// the same entry-point names and argument order (PagedAttentionGemvCuda,
+// PagedAttentionGemmCuda) and the same attributes (kMaxKVLenNonSplit,
+// kKVLenPerPage, kDimHead), plus StoreKVCacheCuda for the slot-mapped KV write
+// the reference does in Python.  Each function validates like the reference's
+// TORCH_CHECKs (csrc/paged_attention/paged_attention_gemv.cu:231-274,
+// paged_attention_gemm.cu:314-358), allocates the output (and the split-KV
+// workspace) with the caching allocator, and calls the C ABI on the current
+// CUDA stream.  The same functions are also registered as torch.ops.femtovllm_b200.*.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime_api.h>
+#include <torch/extension.h>
+
+#include "femtovllm_b200.h"
+
+namespace {
+
+int dtype_code(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat:
+      return FVB_DTYPE_F32;
+    case at::kBFloat16:
+      return FVB_DTYPE_BF16;
+    case at::kHalf:
+      return FVB_DTYPE_F16;
+    default:
+      TORCH_CHECK(false, "femtovllm_b200: unsupported dtype ", t, " (float32, bfloat16, float16)");
+  }
+  return -1;
+}
+
+void check_status(int st, const char* what) {
+  if (st == FVB_OK) return;
+  if (st == FVB_ERR_CUDA) {
+    const int ce = fvb_last_cuda_error();
+    TORCH_CHECK(false, what, " failed: ", fvb_status_string(st), " (", cudaGetErrorString(cudaError_t(ce)), ")");
+  }
+  TORCH_CHECK(false, what, " failed: ", fvb_status_string(st));
+}
+
+void* stream_of(const at::Tensor& t) {
+  return static_cast<void*>(at::cuda::getCurrentCUDAStream(t.get_device()).stream());
+}
+
+void check_pools(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool) {
+  TORCH_CHECK(q.is_cuda() && k_pool.is_cuda() && v_pool.is_cuda(), "q, k_pool and v_pool must be CUDA tensors");
+  TORCH_CHECK(q.is_contiguous() && k_pool.is_contiguous() && v_pool.is_contiguous(),
+              "q, k_pool and v_pool must be contiguous");
+  TORCH_CHECK(q.dim() == 3, "q must be (n_heads, q_len_flatten, d_head)");
+  TORCH_CHECK(k_pool.dim() == 4 && v_pool.dim() == 4, "pools must be (num_blocks, n_kv_heads, block_size, d_head)");
+  TORCH_CHECK(q.size(-1) == k_pool.size(-1) && q.size(-1) == v_pool.size(-1), "d_head mismatch");
+  for (int i = 0; i < 4; ++i) TORCH_CHECK(k_pool.size(i) == v_pool.size(i), "k_pool / v_pool shape mismatch");
+  TORCH_CHECK(q.scalar_type() == k_pool.scalar_type() && q.scalar_type() == v_pool.scalar_type(),
+              "q, k_pool and v_pool must share a dtype");
+  TORCH_CHECK(q.get_device() == k_pool.get_device() && q.get_device() == v_pool.get_device(),
+              "q and the pools must be on one device");
+}
+
+}  // namespace
+
+torch::Tensor PagedAttentionGemvCuda(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
+                                     torch::Tensor kv_page_tables, torch::Tensor kv_lens, int64_t max_kv_len) {
+  check_pools(q, k_pool, v_pool);
+  TORCH_CHECK(kv_page_tables.scalar_type() == torch::kInt32 && kv_lens.scalar_type() == torch::kInt32,
+              "kv_page_tables and kv_lens must be int32");
+  TORCH_CHECK(kv_page_tables.is_cuda() && kv_lens.is_cuda(), "kv_page_tables and kv_lens must be CUDA tensors");
+  TORCH_CHECK(kv_page_tables.dim() == 2 && kv_page_tables.is_contiguous(), "kv_page_tables must be (B, max_blocks)");
+  TORCH_CHECK(kv_lens.is_contiguous(), "kv_lens must be contiguous");
+  const int n_heads = int(q.size(0));
+  const int num_seqs = int(q.size(1));
+  const int head_dim = int(q.size(2));
+  TORCH_CHECK(kv_page_tables.size(0) == num_seqs && kv_lens.numel() == num_seqs,
+              "one block table row and one kv_len per sequence");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty_like(q);
+  const size_t ws_bytes = fvb_paged_attention_decode_workspace_size(num_seqs, n_heads, int(k_pool.size(1)), head_dim,
+                                                                    int(max_kv_len));
+  torch::Tensor ws;
+  if (ws_bytes > 0) ws = torch::empty({int64_t(ws_bytes)}, q.options().dtype(torch::kUInt8));
+  check_status(fvb_paged_attention_decode(q.data_ptr(), out.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+                                          k_pool.size(0), n_heads, int(k_pool.size(1)), head_dim,
+                                          int(k_pool.size(2)), num_seqs, kv_page_tables.data_ptr<int32_t>(),
+                                          int(kv_page_tables.size(1)), kv_lens.data_ptr<int32_t>(), int(max_kv_len),
+                                          dtype_code(q.scalar_type()), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes,
+                                          stream_of(q)),
+               "PagedAttentionGemvCuda");
+  return out;
+}
+
+torch::Tensor PagedAttentionGemmCuda(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
+                                     torch::Tensor cu_seqlens, int64_t max_q_len, torch::Tensor kv_page_tables,
+                                     torch::Tensor kv_lens, torch::Tensor positions) {
+  check_pools(q, k_pool, v_pool);
+  for (const auto* t : {&cu_seqlens, &kv_page_tables, &kv_lens, &positions}) {
+    TORCH_CHECK(t->scalar_type() == torch::kInt32, "metadata tensors must be int32");
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous(), "metadata tensors must be contiguous CUDA tensors");
+  }
+  const int num_seqs = int(cu_seqlens.numel()) - 1;
+  TORCH_CHECK(num_seqs >= 0, "cu_seqlens must have num_seqs + 1 entries");
+  TORCH_CHECK(kv_page_tables.dim() == 2 && kv_page_tables.size(0) == num_seqs, "kv_page_tables must be (B, max_blocks)");
+  TORCH_CHECK(kv_lens.numel() == num_seqs, "one kv_len per sequence");
+  const int n_heads = int(q.size(0));
+  const int64_t q_len_flatten = q.size(1);
+  const int head_dim = int(q.size(2));
+  TORCH_CHECK(positions.numel() == q_len_flatten, "one position per query token");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty({n_heads, q_len_flatten, head_dim}, q.options());
+  const size_t ws_bytes = fvb_paged_attention_prefill_workspace_size(num_seqs, n_heads, int(k_pool.size(1)), head_dim,
+                                                                     q_len_flatten, int(max_q_len));
+  torch::Tensor ws;
+  if (ws_bytes > 0) ws = torch::empty({int64_t(ws_bytes)}, q.options().dtype(torch::kUInt8));
+  check_status(fvb_paged_attention_prefill(q.data_ptr(), out.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+                                           k_pool.size(0), n_heads, int(k_pool.size(1)), head_dim,
+                                           int(k_pool.size(2)), num_seqs, q_len_flatten,
+                                           cu_seqlens.data_ptr<int32_t>(), int(max_q_len),
+                                           kv_page_tables.data_ptr<int32_t>(), int(kv_page_tables.size(1)),
+                                           kv_lens.data_ptr<int32_t>(), positions.data_ptr<int32_t>(),
+                                           dtype_code(q.scalar_type()), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes,
+                                           stream_of(q)),
+               "PagedAttentionGemmCuda");
+  return out;
+}
+
+void StoreKVCacheCuda(torch::Tensor k, torch::Tensor v, torch::Tensor k_pool, torch::Tensor v_pool,
+                      torch::Tensor slot_mapping) {
+  TORCH_CHECK(k.is_cuda() && v.is_cuda() && k_pool.is_cuda() && v_pool.is_cuda() && slot_mapping.is_cuda(),
+              "all arguments must be CUDA tensors");
+  TORCH_CHECK(k.dim() == 3 && v.dim() == 3, "k and v must be (num_tokens, n_kv_heads, d_head)");
+  TORCH_CHECK(k.sizes() == v.sizes() && k.strides() == v.strides(), "k and v must have one shape and stride");
+  TORCH_CHECK(k.stride(2) == 1, "d_head must be the contiguous dimension of k and v");
+  TORCH_CHECK(k_pool.dim() == 4 && k_pool.sizes() == v_pool.sizes(), "pools must be (num_blocks, Hkv, 16, d_head)");
+  TORCH_CHECK(k_pool.is_contiguous() && v_pool.is_contiguous(), "pools must be contiguous");
+  TORCH_CHECK(k_pool.size(1) == k.size(1) && k_pool.size(3) == k.size(2), "pool and k head shapes differ");
+  TORCH_CHECK(k.scalar_type() == k_pool.scalar_type() && v.scalar_type() == v_pool.scalar_type() &&
+                  k.scalar_type() == v.scalar_type(),
+              "k, v and the pools must share a dtype");
+  TORCH_CHECK(slot_mapping.scalar_type() == torch::kInt64 && slot_mapping.is_contiguous() &&
+                  slot_mapping.numel() == k.size(0),
+              "slot_mapping must be a contiguous int64 tensor with one entry per token");
+  c10::cuda::CUDAGuard guard(k.device());
+  check_status(fvb_store_kvcache(k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k_pool.data_ptr(),
+                                 v_pool.data_ptr(), k_pool.size(0), slot_mapping.data_ptr<int64_t>(), k.size(0),
+                                 int(k.size(1)), int(k.size(2)), int(k_pool.size(2)), dtype_code(k.scalar_type()),
+                                 stream_of(k)),
+               "StoreKVCacheCuda");
+}
+
+std::tuple<int64_t, int64_t> ReadDeviceError() {
+  int code = 0, info = 0;
+  check_status(fvb_read_device_error(&code, &info,
+                                     static_cast<void*>(at::cuda::getCurrentCUDAStream().stream())),
+               "ReadDeviceError");
+  return {code, info};
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.attr("kMaxKVLenNonSplit") = fvb_max_kv_len();
+  m.attr("kKVLenPerPage") = fvb_kv_len_per_page();
+  m.attr("kDimHead") = fvb_dim_head();
+  m.def("PagedAttentionGemvCuda", &PagedAttentionGemvCuda, "decode paged attention (split-KV, sm_100a)");
+  m.def("PagedAttentionGemmCuda", &PagedAttentionGemmCuda, "varlen chunked-prefill paged attention (sm_100a)");
+  m.def("StoreKVCacheCuda", &StoreKVCacheCuda, "slot-mapped KV-cache write");
+  m.def("ReadDeviceError", &ReadDeviceError, "read and clear the device error word (synchronizes)");
+}
+
+TORCH_LIBRARY(femtovllm_b200, m) {
+  m.def(
+      "paged_attention_decode(Tensor q, Tensor k_pool, Tensor v_pool, Tensor block_tables, Tensor kv_lens, "
+      "int max_kv_len) -> Tensor");
+  m.def(
+      "paged_attention_prefill(Tensor q, Tensor k_pool, Tensor v_pool, Tensor cu_seqlens, int max_q_len, "
+      "Tensor block_tables, Tensor kv_lens, Tensor positions) -> Tensor");
+  m.def("store_kvcache(Tensor k, Tensor v, Tensor(a!) k_pool, Tensor(b!) v_pool, Tensor slot_mapping) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
+  m.impl("paged_attention_decode", &PagedAttentionGemvCuda);
+  m.impl("paged_attention_prefill", &PagedAttentionGemmCuda);
+  m.impl("store_kvcache", &StoreKVCacheCuda);
+}

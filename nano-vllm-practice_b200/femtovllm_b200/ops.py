@@ -1,0 +1,127 @@
+"""Python op boundary, mirroring ``femtovllm/ops/__init__.py`` of the reference.
+
+Same function names, argument order and meaning, and error behaviour:
+
+* ``paged_attention_gemv`` (reference ``ops/__init__.py:82-107``): decode,
+  ``q`` of shape ``(n_heads, B, d_head)``;
+* ``paged_attention_gemm`` (reference ``ops/__init__.py:110-156``): varlen
+  chunked prefill, ``q`` of shape ``(n_heads, q_len_flatten, d_head)``;
+* ``MAX_KV_LEN_NON_SPLIT``, ``KV_LEN_PER_PAGE``, ``DIM_HEAD`` (reference
+  ``ops/__init__.py:21-26``), read from the native module;
+
+plus ``store_kvcache``, the slot-mapped KV write that replaces the Python
+loops of ``femtovllm/models/qwen/qwen3.py:240-264, 322-366``.
+
+The reference routes each op through a Triton/CUDA backend switch
+(``femtovllm._DEV``, ``ImplCustomKernel``).  That router is gone: ``impl`` is
+accepted for signature compatibility and ignored; every call runs the sm_100a
+kernels of ``libfemtovllm_b200.so``.  Non-CUDA tensors raise ``ValueError``
+(reference ``ops/__init__.py:36-39``); the native checks raise
+``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from femtovllm_b200 import EXT_PATH
+
+try:
+    from femtovllm_b200 import _C as _cuda_backend
+except ImportError as e:  # no fallback: the product path is the CUDA extension
+    raise ImportError(
+        f"femtovllm_b200: native extension not built ({EXT_PATH}). "
+        "Run `python -m femtovllm_b200._build` from nano-vllm-practice_b200/."
+    ) from e
+
+MAX_KV_LEN_NON_SPLIT = _cuda_backend.kMaxKVLenNonSplit
+KV_LEN_PER_PAGE = _cuda_backend.kKVLenPerPage
+DIM_HEAD = _cuda_backend.kDimHead
+
+
+def _ensure_valid_tensor(t: torch.Tensor, name: str) -> torch.Tensor:
+    """CUDA check + contiguous copy, as the reference helper (ops/__init__.py:29-44)."""
+    if not t.is_cuda:
+        raise ValueError(f"Argument '{name}' must be a CUDA tensor. Got device={t.device}")
+    if not t.is_contiguous():
+        return t.contiguous()
+    return t
+
+
+def paged_attention_gemv(
+    q: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    kv_page_tables: torch.Tensor,
+    kv_lens: torch.Tensor,
+    max_kv_len: int,
+    impl=None,
+) -> torch.Tensor:
+    """Decode paged attention; returns ``(n_heads, B, d_head)`` in q's dtype."""
+    q = _ensure_valid_tensor(q, "q")
+    for t, n in ((k_pool, "k_pool"), (v_pool, "v_pool"), (kv_page_tables, "kv_page_tables"), (kv_lens, "kv_lens")):
+        if not t.is_cuda:
+            raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
+    return _cuda_backend.PagedAttentionGemvCuda(q, k_pool, v_pool, kv_page_tables, kv_lens, int(max_kv_len))
+
+
+def paged_attention_gemm(
+    q: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    max_q_len: int,
+    Q_TILE_SIZE: int,
+    cu_q_tiles: torch.Tensor,
+    q_tile_to_seq_idx: torch.Tensor,
+    kv_page_tables: torch.Tensor,
+    kv_lens: torch.Tensor,
+    positions: torch.Tensor,
+    impl=None,
+) -> torch.Tensor:
+    """Varlen chunked-prefill attention; returns ``(n_heads, q_len_flatten, d_head)``.
+
+    ``Q_TILE_SIZE``, ``cu_q_tiles`` and ``q_tile_to_seq_idx`` are the
+    reference Triton kernel's tiling metadata (``model_runner.py:174-202``);
+    they are accepted and unused, since the kernel tiles the queries itself.
+    """
+    q = _ensure_valid_tensor(q, "q")
+    for t, n in (
+        (k_pool, "k_pool"),
+        (v_pool, "v_pool"),
+        (cu_seqlens, "cu_seqlens"),
+        (kv_page_tables, "kv_page_tables"),
+        (kv_lens, "kv_lens"),
+        (positions, "positions"),
+    ):
+        if not t.is_cuda:
+            raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
+    return _cuda_backend.PagedAttentionGemmCuda(
+        q, k_pool, v_pool, cu_seqlens, int(max_q_len), kv_page_tables, kv_lens, positions
+    )
+
+
+def store_kvcache(
+    k: torch.Tensor,
+    v: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    slot_mapping: torch.Tensor,
+) -> None:
+    """Write ``k[t]``, ``v[t]`` (each ``(n_kv_heads, d_head)``) to pool slot ``slot_mapping[t]``.
+
+    ``slot = block_table[s][pos // 16] * 16 + pos % 16`` (int64; ``-1`` skips).
+    ``k`` / ``v`` may be strided views ``(T, n_kv_heads, d_head)`` of the
+    projection output as long as ``d_head`` is contiguous.
+    """
+    for t, n in ((k, "k"), (v, "v"), (k_pool, "k_pool"), (v_pool, "v_pool"), (slot_mapping, "slot_mapping")):
+        if not t.is_cuda:
+            raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
+    if slot_mapping.dtype != torch.int64:
+        slot_mapping = slot_mapping.to(torch.int64)
+    _cuda_backend.StoreKVCacheCuda(k, v, k_pool, v_pool, slot_mapping.contiguous())
+
+
+def read_device_error() -> tuple[int, int]:
+    """(code, info) of the first bad page / slot / timeout a kernel recorded; clears it. Synchronizes."""
+    return tuple(_cuda_backend.ReadDeviceError())

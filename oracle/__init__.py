@@ -1,0 +1,32 @@
+"""CPU oracle for the FemtoVLLM attention hot path.
+
+TEST INFRASTRUCTURE ONLY.  This package restates, in numpy, the reference
+algorithm of fishAndShrimp/nano-vllm-practice ("FemtoVLLM") for the three
+parts of the attention hot path:
+
+* the KV-cache write (the reference's per-sequence block-walk loops, and the
+  equivalent ``slot_mapping`` scatter),
+* decode paged attention over ``block_tables`` with GQA,
+* varlen chunked-prefill causal attention over prefix-cached paged KV.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
+``--impl reference`` legs of ``bench.py`` may import it, and only as the
+checker or the timed CPU baseline.  The product path
+(``femtovllm_b200``) never imports it and has no CPU fallback.
+
+Parity pin: ``tests/golden/*.npz`` were produced by running the reference's
+own ``QwenSelfAttention.forward_varlen_pytorch`` and its KV-write loops
+(``femtovllm/models/qwen/qwen3.py:240-264, 322-366, 389-544``) on CPU, by
+``tests/golden/make_golden.py``.  ``tests/test_oracle_golden.py`` checks this
+package against every one of those fixtures.
+"""
+
+from oracle.paged_attention import (  # noqa: F401
+    build_slot_mapping,
+    decode_attention,
+    gather_seq_kv,
+    prefill_attention,
+    store_kvcache,
+    store_kvcache_decode_loop,
+    store_kvcache_prefill_loop,
+)

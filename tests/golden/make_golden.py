@@ -1,0 +1,274 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Usage (needs the fishAndShrimp/nano-vllm-practice source tree, CPU only):
+
+    python tests/golden/make_golden.py --reference <path to the reference tree>
+
+The reference package imports on CPU once ``femtovllm._C`` is a stub module
+carrying its three constants (kMaxKVLenNonSplit, kKVLenPerPage, kDimHead;
+``csrc/bindings.cpp:62-66``), since ``femtovllm/ops/__init__.py:6-26`` is its
+only hard dependency on the native module.  For every case this script
+builds a ``QwenSelfAttention`` (``femtovllm/models/qwen/qwen3.py:141``) whose
+projections slice a packed input ``x = [q | k | v]``, whose q/k norms, RoPE
+and o_proj are identities, and runs:
+
+* ``forward_varlen_pytorch`` (``qwen3.py:389-544``): the reference KV write
+  plus per-sequence page gather, GQA replication and SDPA with the
+  right-bottom mask -> ``out`` and the pools after the write;
+* the KV-write loop of ``forward_varlen_custom_gemv`` (decode,
+  ``qwen3.py:240-264``) or ``forward_varlen_custom_gemm`` (prefill,
+  ``qwen3.py:322-366``), with the attention op replaced by a stub -> the pools
+  after that loop.
+
+All values are bf16-representable (stored as bf16 bits) so one fixture serves
+both the fp32 and the bf16 checks; the reference runs in fp32.  Each fixture
+stores the pools before the write and only the rows the reference changed.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+PAGE = 16
+
+
+def _import_reference(ref: Path):
+    stub = types.ModuleType("femtovllm._C")
+    stub.kMaxKVLenNonSplit = 8192
+    stub.kKVLenPerPage = 16
+    stub.kDimHead = 128
+    sys.modules["femtovllm._C"] = stub
+    sys.path.insert(0, str(ref))
+    import femtovllm  # noqa: F401
+    import femtovllm.ops
+    from femtovllm.models.qwen.qwen3 import QwenSelfAttention
+    from femtovllm.protocol import VarlenAttnMetadata
+
+    return femtovllm, QwenSelfAttention, VarlenAttnMetadata
+
+
+class _Slice(torch.nn.Module):
+    def __init__(self, a, b):
+        super().__init__()
+        self.a, self.b = a, b
+
+    def forward(self, x):
+        return x[:, self.a : self.b]
+
+
+class _NoRope(torch.nn.Module):
+    def forward(self, x, positions=None):
+        return x
+
+
+def _bf16_vals(gen, shape, scale=1.0):
+    return (torch.randn(shape, generator=gen) * scale).to(torch.bfloat16).to(torch.float32)
+
+
+def _make_case(name, kv_lens, q_lens, Hq, Hkv, D, num_blocks, tables, seed, scale=1.0):
+    kv_lens = np.asarray(kv_lens, np.int32)
+    q_lens = np.asarray(q_lens, np.int32)
+    gen = torch.Generator().manual_seed(seed)
+    T = int(q_lens.sum())
+    return {
+        "name": name,
+        "Hq": Hq,
+        "Hkv": Hkv,
+        "D": D,
+        "kv_lens": kv_lens,
+        "q_lens": q_lens,
+        "tables": tables,
+        "num_blocks": num_blocks,
+        "q": _bf16_vals(gen, (Hq, T, D), scale),
+        "k_new": _bf16_vals(gen, (T, Hkv, D), scale),
+        "v_new": _bf16_vals(gen, (T, Hkv, D), scale),
+        "k_pool": _bf16_vals(gen, (num_blocks, Hkv, PAGE, D), scale),
+        "v_pool": _bf16_vals(gen, (num_blocks, Hkv, PAGE, D), scale),
+    }
+
+
+def _random_tables(rng, kv_lens, num_blocks, shared=None):
+    perm = list(rng.permutation(num_blocks))
+    head = [] if shared is None else list(shared)
+    perm = [b for b in perm if b not in set(head)]
+    rows = []
+    for kl in kv_lens:
+        n = (int(kl) + PAGE - 1) // PAGE - len(head)
+        rows.append(head + [int(x) for x in perm[:n]])
+        perm = perm[n:]
+    return rows
+
+
+def cases():
+    out = []
+    # 1. BASELINE config 1 shape: decode, B=4, Hq=8, Hkv=2, D=64, context U[1,256] + 1 new token, pool 128.
+    rng = np.random.default_rng(1)
+    ctx = rng.integers(1, 257, size=4)
+    kv = ctx + 1
+    tables = _random_tables(rng, kv, 128)
+    out.append(_make_case("cfg1_decode", kv, [1] * 4, 8, 2, 64, 128, tables, 11))
+    # 2. Reference GEMV test structure (csrc/paged_attention/test_paged_attention_gemv.py:22-50) at page 16:
+    #    tables [[0,4,5,6],[1,8,9]], kv_lens [59,44], Hq 8 / Hkv 4, D 128.
+    out.append(_make_case("toy_decode", [59, 44], [1, 1], 8, 4, 128, 10, [[0, 4, 5, 6], [1, 8, 9]], 12))
+    # 3. Reference Triton prefill test structure (ops/triton/paged_attention/test_paged_attention_gemm.py:18-102):
+    #    cu_seqlens [0,8,24], kv_lens [59,44], same tables.
+    out.append(_make_case("toy_prefill", [59, 44], [8, 16], 8, 4, 128, 10, [[0, 4, 5, 6], [1, 8, 9]], 13))
+    # 4. Chunked prefill over cached prefixes, page-boundary edges, GQA 2.
+    rng = np.random.default_rng(4)
+    c = np.array([1, 17, 33, 64, 100])
+    p = np.array([0, 15, 16, 47, 200])
+    tables = _random_tables(rng, p + c, 40)
+    out.append(_make_case("chunked_prefix_gqa2", p + c, c, 4, 2, 128, 40, tables, 14))
+    # 5. Mixed decode + prefill sharing a 32-token (2-block) prefix, GQA 4.
+    rng = np.random.default_rng(5)
+    q_lens = np.array([1, 20, 1, 1, 37, 1])
+    suffix = np.array([5, 0, 16, 31, 3, 60])
+    kv = 32 + suffix + q_lens
+    tables = _random_tables(rng, kv, 24, shared=[7, 3])
+    out.append(_make_case("mixed_shared_prefix_gqa4", kv, q_lens, 8, 2, 128, 24, tables, 15))
+    # 6. GQA 8, D 64, ragged chunks incl. a 1-token prefill row.
+    rng = np.random.default_rng(6)
+    c = np.array([5, 40, 1])
+    p = np.array([10, 0, 70])
+    tables = _random_tables(rng, p + c, 12)
+    out.append(_make_case("gqa8_d64", p + c, c, 8, 1, 64, 12, tables, 16))
+    # 7. MHA (GQA 1), D 64, decode with kv_len 1 and exact page multiples.
+    rng = np.random.default_rng(7)
+    kv = np.array([1, 16, 32, 17])
+    tables = _random_tables(rng, kv, 8)
+    out.append(_make_case("mha_d64_decode_edges", kv, [1] * 4, 4, 4, 64, 8, tables, 17))
+    return out
+
+
+def run_reference(case, femtovllm, QwenSelfAttention, VarlenAttnMetadata):
+    Hq, Hkv, D = case["Hq"], case["Hkv"], case["D"]
+    kv_lens, q_lens = case["kv_lens"], case["q_lens"]
+    B = len(kv_lens)
+    T = int(q_lens.sum())
+    raw_cu = [0] + np.cumsum(q_lens).tolist()
+    raw_pos = []
+    for kl, ql in zip(kv_lens, q_lens):
+        raw_pos.extend(range(int(kl) - int(ql), int(kl)))
+    raw_tables = [list(map(int, t)) for t in case["tables"]]
+    width = max(len(t) for t in raw_tables)
+    padded = [t + [-1] * (width - len(t)) for t in raw_tables]
+    is_decoding = bool((q_lens == 1).all())
+
+    cfg = types.SimpleNamespace(head_dim=D, rms_norm_eps=1e-6)
+    d_model = D * (Hq + 2 * Hkv)
+    attn = QwenSelfAttention(d_model, Hq, Hkv, max_seqlen=4, dropout_p=0.0, config=cfg)
+    attn.w_q = _Slice(0, Hq * D)
+    attn.w_k = _Slice(Hq * D, (Hq + Hkv) * D)
+    attn.w_v = _Slice((Hq + Hkv) * D, (Hq + 2 * Hkv) * D)
+    attn.q_norm = torch.nn.Identity()
+    attn.k_norm = torch.nn.Identity()
+    attn.rotary_embd = _NoRope()
+    attn.o_proj = torch.nn.Identity()
+    attn.eval()
+
+    q_tok = case["q"].transpose(0, 1).reshape(T, Hq * D)
+    x = torch.cat([q_tok, case["k_new"].reshape(T, Hkv * D), case["v_new"].reshape(T, Hkv * D)], dim=1)
+    Q_TILE = 32
+    cu_tiles, tile_seq = [0], []
+    for s, ql in enumerate(q_lens):
+        n = (int(ql) + Q_TILE - 1) // Q_TILE
+        cu_tiles.append(cu_tiles[-1] + n)
+        tile_seq += [s] * n
+    md = VarlenAttnMetadata(
+        positions=torch.tensor(raw_pos, dtype=torch.int32),
+        raw_positions=raw_pos,
+        cu_seqlens=torch.tensor(raw_cu, dtype=torch.int32),
+        raw_cu_seqlens=raw_cu,
+        max_q_len=int(q_lens.max()),
+        Q_TILE_SIZE=Q_TILE,
+        raw_cu_q_tiles=cu_tiles,
+        cu_q_tiles=torch.tensor(cu_tiles, dtype=torch.int32),
+        raw_q_tile_to_seq_idx=tile_seq,
+        q_tile_to_seq_idx=torch.tensor(tile_seq, dtype=torch.int32),
+        k_cache_pools=None,
+        v_cache_pools=None,
+        kv_lens=torch.tensor(kv_lens, dtype=torch.int32),
+        max_kv_len=int(kv_lens.max()),
+        block_tables=torch.tensor(padded, dtype=torch.int32),
+        raw_block_tables=raw_tables,
+        is_decoding=is_decoding,
+    )
+    kp, vp = case["k_pool"].clone(), case["v_pool"].clone()
+    with torch.no_grad():
+        o, _ = attn.forward_varlen_pytorch(x, kp, vp, md)
+    out = o.reshape(T, Hq, D).transpose(0, 1).contiguous()
+
+    # The custom-kernel routes' own KV-write loops, with the attention op stubbed out.
+    kp2, vp2 = case["k_pool"].clone(), case["v_pool"].clone()
+    stub = lambda q, **kw: torch.zeros_like(q)  # noqa: E731
+    saved = (femtovllm.ops.paged_attention_gemv, femtovllm.ops.paged_attention_gemm)
+    femtovllm.ops.paged_attention_gemv = stub
+    femtovllm.ops.paged_attention_gemm = stub
+    try:
+        with torch.no_grad():
+            if is_decoding:
+                attn.forward_varlen_custom_gemv(x, kp2, vp2, md)
+            else:
+                attn.forward_varlen_custom_gemm(x, kp2, vp2, md)
+    finally:
+        femtovllm.ops.paged_attention_gemv, femtovllm.ops.paged_attention_gemm = saved
+    return out, (kp, vp), (kp2, vp2), padded, raw_cu, raw_pos
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+def _changed_rows(before, after):
+    diff = (before != after).any(dim=-1).nonzero().numpy().astype(np.int32)  # (n, 3): block, head, offset
+    rows = after[diff[:, 0], diff[:, 1], diff[:, 2]]
+    return diff, _bits(rows)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, type=Path)
+    args = ap.parse_args()
+    femtovllm, QSA, VAM = _import_reference(args.reference)
+    for case in cases():
+        out, (kp, vp), (kp2, vp2), padded, cu, pos = run_reference(case, femtovllm, QSA, VAM)
+        k_rows_idx, k_rows = _changed_rows(case["k_pool"], kp)
+        v_rows_idx, v_rows = _changed_rows(case["v_pool"], vp)
+        k2_idx, k2 = _changed_rows(case["k_pool"], kp2)
+        v2_idx, v2 = _changed_rows(case["v_pool"], vp2)
+        assert np.array_equal(k_rows_idx, k2_idx) and np.array_equal(k_rows, k2), "write loops disagree (K)"
+        assert np.array_equal(v_rows_idx, v2_idx) and np.array_equal(v_rows, v2), "write loops disagree (V)"
+        np.savez_compressed(
+            HERE / f"{case['name']}.npz",
+            n_heads=case["Hq"],
+            n_kv_heads=case["Hkv"],
+            head_dim=case["D"],
+            num_blocks=case["num_blocks"],
+            kv_lens=case["kv_lens"],
+            q_lens=case["q_lens"],
+            cu_seqlens=np.asarray(cu, np.int32),
+            positions=np.asarray(pos, np.int32),
+            block_tables=np.asarray(padded, np.int32),
+            q_bits=_bits(case["q"]),
+            k_new_bits=_bits(case["k_new"]),
+            v_new_bits=_bits(case["v_new"]),
+            k_pool_bits=_bits(case["k_pool"]),
+            v_pool_bits=_bits(case["v_pool"]),
+            k_written_idx=k_rows_idx,
+            k_written_bits=k_rows,
+            v_written_idx=v_rows_idx,
+            v_written_bits=v_rows,
+            out_ref=out.numpy().astype(np.float32),
+        )
+        print(f"{case['name']}: T={int(case['q_lens'].sum())} rows written={len(k_rows_idx)}")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,281 @@
+"""GPU parity of the C ABI against the oracle and the reference's golden outputs.
+
+Tolerances (vs an fp32-or-wider reference): KV writes and slot indexing
+bit-exact; fp32 attention max-abs <= 1e-4; bf16 / f16 attention max-abs <= 2e-2
+and mean-abs <= 2e-3.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cabi
+import oracle
+from conftest import GOLDEN_CASES, golden_after, load_golden
+from femtovllm_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: (1e-4, 1e-4), torch.bfloat16: (2e-2, 2e-3), torch.float16: (2e-2, 2e-3)}
+
+
+def assert_close(out: torch.Tensor, ref: np.ndarray, dtype, what=""):
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    err = np.abs(got - ref)
+    max_tol, mean_tol = TOL[dtype]
+    assert err.max() <= max_tol, f"{what}: max abs {err.max():.3g} > {max_tol}"
+    assert err.mean() <= mean_tol, f"{what}: mean abs {err.mean():.3g} > {mean_tol}"
+
+
+def _dev(a, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t.to(dtype) if dtype is not None else t
+
+
+# ---------------------------------------------------------------------------
+# golden fixtures (made by running the reference itself)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_golden_store_then_attend(name, dtype, cuda_device):
+    d = load_golden(name)
+    dev = cuda_device
+    kp, vp = _dev(d["k_pool"], dev, dtype), _dev(d["v_pool"], dev, dtype)
+    slots = _dev(oracle.build_slot_mapping(d["positions"], d["seq_of_token"], d["block_tables"]), dev)
+    cabi.store_kvcache(_dev(d["k_new"], dev, dtype), _dev(d["v_new"], dev, dtype), kp, vp, slots)
+    torch.cuda.synchronize()
+    # bit-exact against the rows the reference's write loop produced
+    assert torch.equal(kp.cpu(), torch.from_numpy(golden_after(d, "k")).to(dtype))
+    assert torch.equal(vp.cpu(), torch.from_numpy(golden_after(d, "v")).to(dtype))
+    q = _dev(d["q"], dev, dtype)
+    tables = _dev(d["block_tables"], dev)
+    kv_lens = _dev(d["kv_lens"], dev)
+    if d["is_decode"]:
+        out = cabi.decode(q, kp, vp, tables, kv_lens, int(d["kv_lens"].max()))
+        assert_close(out, d["out_ref"], dtype, f"{name} decode")
+    out = cabi.prefill(q, kp, vp, _dev(d["cu_seqlens"], dev), int(d["q_lens"].max()), tables, kv_lens,
+                       _dev(d["positions"], dev))
+    assert_close(out, d["out_ref"], dtype, f"{name} prefill")
+    assert cabi.read_device_error() == (0, 0)
+
+
+# ---------------------------------------------------------------------------
+# seeded sweeps against the oracle
+# ---------------------------------------------------------------------------
+
+DECODE_LENS = [1, 2, 15, 16, 17, 31, 32, 33, 64, 100, 257, 1000, 2049, 5000]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("n_rep", [1, 2, 4, 8])
+def test_decode_sweep(dtype, head_dim, n_rep, cuda_device):
+    hkv = 2
+    rng = np.random.default_rng(head_dim * 10 + n_rep)
+    lens = rng.permutation(DECODE_LENS)
+    b = workloads.custom(lens, np.ones(len(lens)), hkv * n_rep, hkv, head_dim, dtype, seed=n_rep).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    ref = oracle.decode_attention(b.q.float().cpu().numpy(), b.k_pool.float().cpu().numpy(),
+                                  b.v_pool.float().cpu().numpy(), b.block_tables, b.kv_lens)
+    assert_close(out, ref, dtype, f"decode {dtype} D{head_dim} rep{n_rep}")
+
+
+def test_decode_without_splits_writes_directly(cuda_device):
+    # Many (seq, kv head) units and short contexts: the plan uses one split per sequence.
+    lens = np.random.default_rng(0).integers(1, 900, size=300)
+    b = workloads.custom(lens, np.ones(300), 16, 8, 128, torch.bfloat16, seed=5).materialize(cuda_device)
+    assert cabi.lib().fvb_paged_attention_decode_workspace_size(300, 16, 8, 128, b.max_kv_len) == 0
+    md = b.device_metadata(cuda_device)
+    out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    sub = [0, 1, 2, int(np.argmax(lens)), int(np.argmin(lens))]
+    ref = oracle.decode_attention(b.q[:, sub].float().cpu().numpy(), b.k_pool.float().cpu().numpy(),
+                                  b.v_pool.float().cpu().numpy(), b.block_tables[sub], b.kv_lens[sub])
+    assert_close(out[:, sub], ref, torch.bfloat16, "no-split decode")
+
+
+PREFILL_CASES = [
+    # (q_lens, prefixes)
+    ([1, 1, 1], [0, 15, 300]),
+    ([5, 16, 17, 31], [0, 0, 3, 16]),
+    ([128, 64, 200], [0, 77, 1000]),
+    ([300, 1, 129], [5000, 40, 0]),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("n_rep", [1, 2, 4, 8])
+@pytest.mark.parametrize("case", range(len(PREFILL_CASES)))
+def test_prefill_sweep(dtype, head_dim, n_rep, case, cuda_device):
+    q_lens, pre = map(np.asarray, PREFILL_CASES[case])
+    hkv = 2
+    b = workloads.custom(q_lens + pre, q_lens, hkv * n_rep, hkv, head_dim, dtype, seed=case).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    out = cabi.prefill(b.q, b.k_pool, b.v_pool, md["cu_seqlens"], b.max_q_len, md["block_tables"], md["kv_lens"],
+                       md["positions"])
+    ref = oracle.prefill_attention(b.q.float().cpu().numpy(), b.k_pool.float().cpu().numpy(),
+                                   b.v_pool.float().cpu().numpy(), b.cu_seqlens, b.block_tables, b.kv_lens,
+                                   b.positions, acc_dtype=np.float32)
+    assert_close(out, ref, dtype, f"prefill case{case} {dtype} D{head_dim} rep{n_rep}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_store_kvcache_sweep_bit_exact(dtype, cuda_device):
+    b = workloads.custom([40, 1, 17, 300], [40, 1, 9, 100], 8, 4, 128, dtype, seed=3).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    kp, vp = b.k_pool.clone(), b.v_pool.clone()
+    # strided views, as the projection outputs are: (T, Hkv * D) viewed as (T, Hkv, D)
+    packed = torch.cat([b.k_new.reshape(b.num_tokens, -1), b.v_new.reshape(b.num_tokens, -1)], dim=1)
+    k = packed[:, : 4 * 128].view(b.num_tokens, 4, 128)
+    v = packed[:, 4 * 128 :].view(b.num_tokens, 4, 128)
+    slots = md["slot_mapping"].clone()
+    slots[3] = -1  # a padding token is skipped
+    cabi.store_kvcache(k, v, kp, vp, slots)
+    kref = b.k_pool.cpu().clone()
+    vref = b.v_pool.cpu().clone()
+    s = slots.cpu().numpy()
+    live = s >= 0
+    kref[s[live] // 16, :, s[live] % 16] = b.k_new.cpu()[live]
+    vref[s[live] // 16, :, s[live] % 16] = b.v_new.cpu()[live]
+    assert torch.equal(kp.cpu(), kref) and torch.equal(vp.cpu(), vref)
+
+
+# ---------------------------------------------------------------------------
+# full-size configurations (sampled oracle checks + size-independent properties)
+# ---------------------------------------------------------------------------
+
+
+def _sample(b, n=6, seed=0):
+    rng = np.random.default_rng(seed)
+    pick = {int(np.argmin(b.kv_lens)), int(np.argmax(b.kv_lens))}
+    while len(pick) < min(n, b.num_seqs):
+        pick.add(int(rng.integers(b.num_seqs)))
+    return sorted(pick)
+
+
+def test_config2_decode_full_size(cuda_device):
+    b = workloads.config2().materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    cabi.store_kvcache(b.k_new, b.v_new, b.k_pool, b.v_pool, md["slot_mapping"])
+    out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    out2 = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    assert torch.equal(out, out2), "decode is not deterministic"
+    seqs = _sample(b)
+    sub = workloads.subset_for_oracle(b, seqs)
+    ref = oracle.decode_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["block_tables"], sub["kv_lens"],
+                                  acc_dtype=np.float32)
+    assert_close(out[:, seqs], ref, torch.bfloat16, "config2")
+    # the new token is visible: its slot now holds k_new
+    s = b.slot_mapping[seqs[0]]
+    assert torch.equal(b.k_pool[s // 16, :, s % 16], b.k_new[seqs[0]])
+    assert cabi.read_device_error() == (0, 0)
+
+
+def test_config5_long_decode_sample(cuda_device):
+    lens = np.array([32768, 131072, 77777, 40001], dtype=np.int32)
+    b = workloads.custom(lens, np.ones(4), 32, 8, 128, torch.bfloat16, seed=55, pool_factor=1.05).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    for s in (0, 1):
+        sub = workloads.subset_for_oracle(b, [s])
+        ref = oracle.decode_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["block_tables"], sub["kv_lens"],
+                                      acc_dtype=np.float32)
+        assert_close(out[:, [s]], ref, torch.bfloat16, f"long decode seq {s}")
+
+
+def test_config3_prefill_full_size(cuda_device):
+    b = workloads.config3().materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    out = cabi.prefill(b.q, b.k_pool, b.v_pool, md["cu_seqlens"], b.max_q_len, md["block_tables"], md["kv_lens"],
+                       md["positions"])
+    # two sequences against the oracle: the shortest total and one random
+    seqs = [int(np.argmin(b.kv_lens)), 7]
+    sub = workloads.subset_for_oracle(b, seqs)
+    ref = oracle.prefill_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["cu_seqlens"], sub["block_tables"],
+                                   sub["kv_lens"], sub["positions"], acc_dtype=np.float32)
+    assert_close(out[:, torch.from_numpy(sub["tokens"]).to(cuda_device)], ref, torch.bfloat16, "config3")
+
+
+def test_config4_mixed_full_size(cuda_device):
+    b = workloads.config4().materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    out = cabi.prefill(b.q, b.k_pool, b.v_pool, md["cu_seqlens"], b.max_q_len, md["block_tables"], md["kv_lens"],
+                       md["positions"])
+    dec = [int(i) for i in np.nonzero(b.q_lens == 1)[0][:3]]
+    pre = [int(np.nonzero(b.q_lens > 1)[0][0])]
+    sub = workloads.subset_for_oracle(b, dec + pre)
+    ref = oracle.prefill_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["cu_seqlens"], sub["block_tables"],
+                                   sub["kv_lens"], sub["positions"], acc_dtype=np.float32)
+    assert_close(out[:, torch.from_numpy(sub["tokens"]).to(cuda_device)], ref, torch.bfloat16, "config4")
+    # decode rows through the decode kernel agree with the unified launch
+    dmask = b.q_lens == 1
+    tok = torch.from_numpy(b.cu_seqlens[:-1][dmask].astype(np.int64)).to(cuda_device)
+    tabs = md["block_tables"][torch.from_numpy(np.nonzero(dmask)[0]).to(cuda_device)].contiguous()
+    lens = md["kv_lens"][torch.from_numpy(np.nonzero(dmask)[0]).to(cuda_device)].contiguous()
+    dout = cabi.decode(b.q[:, tok].contiguous(), b.k_pool, b.v_pool, tabs, lens, int(b.kv_lens[dmask].max()))
+    assert (dout.float() - out[:, tok].float()).abs().max().item() <= 2e-2
+
+
+# ---------------------------------------------------------------------------
+# bad metadata is reported, never read out of bounds
+# ---------------------------------------------------------------------------
+
+
+def test_bad_page_and_slot_are_reported(cuda_device):
+    b = workloads.custom([40, 20], [1, 1], 4, 2, 64, torch.bfloat16, seed=1).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    cabi.read_device_error()
+    tables = md["block_tables"].clone()
+    tables[0, 1] = -1  # a hole inside kv_len
+    cabi.decode(b.q, b.k_pool, b.v_pool, tables, md["kv_lens"], b.max_kv_len)
+    assert cabi.read_device_error()[0] == 7  # FVB_ERR_BAD_PAGE
+    tables[0, 1] = b.num_blocks + 5  # past the pool
+    cabi.prefill(b.q, b.k_pool, b.v_pool, md["cu_seqlens"], 1, tables, md["kv_lens"], md["positions"])
+    assert cabi.read_device_error()[0] == 7
+    slots = md["slot_mapping"].clone()
+    slots[1] = b.num_blocks * 16  # one past the last slot
+    kp = b.k_pool.clone()
+    cabi.store_kvcache(b.k_new, b.v_new, kp, b.v_pool.clone(), slots)
+    assert cabi.read_device_error() == (8, 1)  # FVB_ERR_BAD_SLOT at token 1
+    s0 = int(slots[0])
+    assert torch.equal(kp[s0 // 16, :, s0 % 16], b.k_new[0])  # the good token is still written
+
+
+def test_kv_len_beyond_max_kv_len_is_clamped_and_reported(cuda_device):
+    b = workloads.custom([40, 20], [1, 1], 4, 2, 64, torch.bfloat16, seed=2).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    cabi.read_device_error()
+    cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], 32)  # max_kv_len < kv_lens[0]
+    assert cabi.read_device_error()[0] == 1
+
+
+# ---------------------------------------------------------------------------
+# the PyTorch-registered boundary (femtovllm_b200.ops / torch.ops) = the C ABI
+# ---------------------------------------------------------------------------
+
+
+def test_torch_ops_match_c_abi(cuda_device):
+    from femtovllm_b200 import ops
+
+    b = workloads.custom([70, 33, 200], [1, 1, 1], 8, 2, 128, torch.bfloat16, seed=9).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    kp1, vp1 = b.k_pool.clone(), b.v_pool.clone()
+    ops.store_kvcache(b.k_new, b.v_new, kp1, vp1, md["slot_mapping"])
+    kp2, vp2 = b.k_pool.clone(), b.v_pool.clone()
+    torch.ops.femtovllm_b200.store_kvcache(b.k_new, b.v_new, kp2, vp2, md["slot_mapping"])
+    assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
+    a = ops.paged_attention_gemv(b.q, kp1, vp1, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    c = cabi.decode(b.q, kp1, vp1, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    assert torch.equal(a, c)
+    # transposed (non-contiguous) q is made contiguous, as the reference wrapper does
+    qt = b.q.transpose(0, 1).contiguous().transpose(0, 1)
+    assert torch.equal(ops.paged_attention_gemv(qt, kp1, vp1, md["block_tables"], md["kv_lens"], b.max_kv_len), a)
+    g = ops.paged_attention_gemm(b.q, kp1, vp1, md["cu_seqlens"], 1, 32, None, None, md["block_tables"],
+                                 md["kv_lens"], md["positions"])
+    assert (g.float() - a.float()).abs().max().item() <= 2e-2
+    with pytest.raises(RuntimeError):
+        ops.paged_attention_gemv(b.q.to(torch.float64), kp1, vp1, md["block_tables"], md["kv_lens"], b.max_kv_len)
