@@ -188,7 +188,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    batch = workloads.config2(seed=2 + rank).materialize(dev)
+    batch = workloads.config2(seed=2 + rank, num_seqs=args.num_seqs).materialize(dev)
     md = batch.device_metadata(dev)
     q, kp, vp = batch.q, batch.k_pool, batch.v_pool
     tables, lens, slots = md["block_tables"], md["kv_lens"], md["slot_mapping"]
@@ -297,6 +297,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seqs", type=int, default=24)
+    ap.add_argument("--num-seqs", type=int, default=256, help="sequences per GPU (256 = BASELINE config 2)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
