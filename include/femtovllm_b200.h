@@ -106,6 +106,28 @@ FVB_API int fvb_paged_attention_decode(const void* q, void* out, const void* k_p
                                size_t workspace_bytes, void* stream);
 
 /*
+ * Decode paged attention without a caller-provided workspace.  No counterpart
+ * in the reference.  For callers that cannot allocate device memory when they
+ * call: an engine that has reserved nearly all HBM for its KV block pool, or a
+ * host runtime that may not call cudaMalloc / cudaFree on the decode path
+ * (cudaFree synchronizes the device).  Same arguments and result as
+ * fvb_paged_attention_decode minus the workspace: the split partials live in a
+ * fixed FVB_DECODE_NOALLOC_SCRATCH_BYTES (32 MiB) array inside the library,
+ * which every GPU that loads it holds until the process exits.  A launch whose
+ * partials need more is rejected unrun with FVB_ERR_WORKSPACE_TOO_SMALL.  The
+ * first call on a device looks up the array's device address; make that call
+ * before any stream capture.  All calls on a device share the array (nothing in
+ * it needs to start at zero), so calls whose kernels overlap on the GPU race.
+ * Allocates nothing.
+ */
+#define FVB_DECODE_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+FVB_API int fvb_paged_attention_decode_noalloc(const void* q, void* out, const void* k_pool, const void* v_pool,
+                                               int64_t num_blocks, int n_heads, int n_kv_heads, int head_dim,
+                                               int block_size, int num_seqs, const int32_t* block_tables,
+                                               int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len,
+                                               int dtype, void* stream);
+
+/*
  * Varlen chunked-prefill causal attention over paged, prefix-cached KV.
  *
  * Replaces PagedAttentionGemmCuda (csrc/paged_attention/paged_attention_gemm.cu:304-394,
