@@ -298,6 +298,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seqs", type=int, default=24)
     ap.add_argument("--num-seqs", type=int, default=256, help="sequences per GPU (256 = BASELINE config 2)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long"],
+                    help="decode = config 2 (the contract line); prefill = config 3; mixed = config 4; "
+                         "long = config 5 sharded over the ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -319,6 +322,12 @@ def main():
     if world > 1:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+    if args.workload != "decode":
+        run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     gathered, clocks, decode_bytes, launches, cpu, (h2d, d2h), batch = run_gpu(args, rank, world, local_rank)
     if rank == 0:
         t_step = max(g["step_ms"] for g in gathered)
@@ -377,6 +386,67 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
+    """Development measurements: prefill (config 3), mixed (config 4), long decode (config 5)."""
+    import torch
+    import torch.distributed as dist
+
+    from femtovllm_b200 import ops, workloads
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if args.workload == "prefill":
+        batch = workloads.config3(seed=3 + rank)
+    elif args.workload == "mixed":
+        batch = workloads.config4(seed=4 + rank)
+    else:
+        batch = workloads.config5(rank=rank, world=world)
+    batch.materialize(dev)
+    md = batch.device_metadata(dev)
+    stream = torch.cuda.current_stream()
+    if args.workload == "long":
+        def step():
+            return ops.paged_attention_gemv(batch.q, batch.k_pool, batch.v_pool, md["block_tables"], md["kv_lens"],
+                                            batch.max_kv_len)
+    else:
+        def step():
+            return ops.paged_attention_gemm(batch.q, batch.k_pool, batch.v_pool, md["cu_seqlens"], batch.max_q_len, 32,
+                                            None, None, md["block_tables"], md["kv_lens"], md["positions"])
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    res = {"ms": ms, "flops": batch.attn_flops(), "bytes": batch.decode_bytes() if args.workload == "long"
+           else batch.kv_bytes(), "tokens": batch.num_tokens}
+    gathered = [None] * world
+    if world > 1:
+        dist.all_gather_object(gathered, res)
+    else:
+        gathered = [res]
+    if rank != 0:
+        return
+    t = max(g["ms"] for g in gathered)
+    flops = sum(g["flops"] for g in gathered)
+    nbytes = sum(g["bytes"] for g in gathered)
+    tokens = sum(g["tokens"] for g in gathered)
+    line = {"metric": METRIC, "workload": args.workload, "n_gpus": world, "steps": args.steps, "ms_per_step": round(t, 5),
+            "tflops": round(flops / (t * 1e-3) / 1e12, 2), "gbs": round(nbytes / (t * 1e-3) / 1e9, 1),
+            "tokens_per_s": round(tokens / (t * 1e-3), 1),
+            "pct_tensor_peak": round(100 * flops / (t * 1e-3) / 1e12 / (tflops_peak * world), 2),
+            "pct_hbm_peak": round(100 * nbytes / (t * 1e-3) / 1e9 / (hbm_peak * world), 2),
+            "peak_source": peak_src, "config": batch.name, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
 
 
 def run_reference_arm(args, rank: int, world: int):

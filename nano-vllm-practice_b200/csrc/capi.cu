@@ -213,13 +213,10 @@ int fvb_paged_attention_decode(const void* q, void* out, const void* k_pool, con
 
 size_t fvb_paged_attention_prefill_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
                                                   int64_t q_len_flatten, int max_q_len) {
-  (void)num_seqs;
-  (void)n_heads;
-  (void)n_kv_heads;
-  (void)head_dim;
-  (void)q_len_flatten;
-  (void)max_q_len;
-  return 0;
+  if (num_seqs <= 0 || !gqa_ok(n_heads, n_kv_heads)) return 0;
+  // The tile plan (one int32 per sequence + 1) is the same for bf16 and f16;
+  // the fp32 path needs none but accepts it.
+  return plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, q_len_flatten, max_q_len, FVB_DTYPE_BF16).ws_bytes;
 }
 
 int fvb_paged_attention_prefill(const void* q, void* out, const void* k_pool, const void* v_pool,
@@ -228,20 +225,27 @@ int fvb_paged_attention_prefill(const void* q, void* out, const void* k_pool, co
                                 const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
                                 const int32_t* positions, int dtype, void* workspace, size_t workspace_bytes,
                                 void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   int st = check_attention(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
                            block_tables, max_blocks_per_seq, kv_lens, dtype);
   if (st) return st;
   if (q_len_flatten < 0 || max_q_len < 0) return FVB_ERR_INVALID_ARGUMENT;
   if (num_seqs == 0 || q_len_flatten == 0) return FVB_OK;
   if (!cu_seqlens || !positions) return FVB_ERR_INVALID_ARGUMENT;
+  if (q_len_flatten * n_heads > int64_t(0x7fffffff)) return FVB_ERR_UNSUPPORTED;  // TMA row coordinate of q
   cudaError_t e;
   int* err = device_error_ptr(&e);
   if (!err) return cuda_status(e);
-  return cuda_status(launch_prefill_simt(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
-                                         q_len_flatten, cu_seqlens, block_tables, max_blocks_per_seq, kv_lens,
-                                         positions, dtype, err, static_cast<cudaStream_t>(stream)));
+  if (dtype == FVB_DTYPE_F32) {
+    return cuda_status(launch_prefill_simt(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim,
+                                           num_seqs, q_len_flatten, cu_seqlens, block_tables, max_blocks_per_seq,
+                                           kv_lens, positions, dtype, err, static_cast<cudaStream_t>(stream)));
+  }
+  const PrefillPlan plan = plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, q_len_flatten, max_q_len, dtype);
+  if (!workspace || workspace_bytes < plan.ws_bytes) return FVB_ERR_WORKSPACE_TOO_SMALL;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return FVB_ERR_MISALIGNED;
+  return cuda_status(launch_prefill(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
+                                    q_len_flatten, cu_seqlens, max_q_len, block_tables, max_blocks_per_seq, kv_lens,
+                                    positions, dtype, plan, workspace, err, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"
