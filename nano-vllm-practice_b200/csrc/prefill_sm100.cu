@@ -8,29 +8,32 @@
 // Semantics (the reference's): key j is visible to query i of sequence s iff
 // j < kv_lens[s] and j <= positions[i]; softmax in fp32; output cast to T.
 //
-// Work item = (query tile, kv head).  A tile is 128 rows: 128 / n_rep
-// consecutive query tokens of one sequence x the n_rep query heads of the kv
-// head's GQA group, so every K/V tile fetched serves the whole group.  KV is
-// consumed in 128-key tiles (8 pages).
+// Query tile = 128 rows: 128 / n_rep consecutive query tokens of one sequence
+// x the n_rep query heads of one kv head's GQA group, so every K/V byte
+// fetched serves the whole group.  Work item = (two consecutive query tiles
+// of one sequence, kv head); KV is consumed in 128-key tiles (8 pages).
 //
-//   warp 0      TMA producer: the Q tile once, then for every KV tile the 8
-//               pages of K and of V, page by page through the block table
-//               (2-D tensor maps over the pools viewed as [blocks*Hkv*16, D],
-//               128-byte swizzle), into a ring of kStages K and V slots.
-//   warp 1      owns TMEM (512 columns: S double buffer 2x128, O D columns)
-//               and issues the MMAs from one thread:
-//                 S[j%2] = Q K_j^T   (M=128, N=128, K=D; both K-major in smem)
-//                 O     += P_j V_j   (M=128, N=D,  K=128; P K-major, V MN-major)
-//               S_{j+1} is issued before PV_j so the tensor pipe computes the
-//               next scores while the softmax works on the current ones.
-//   warps 2-5   softmax / epilogue, one thread per tile row (TMEM lane
-//               quarter = warp % 4): read S_j from TMEM, mask, online softmax
-//               in fp32 (log2 domain), rescale O in TMEM when the running max
-//               grows, write P_j (bf16/f16) into a 128-byte-swizzled smem
-//               tile for the PV MMA, and finally O / l -> global.
+//   warpgroup 0  warp 0: TMA producer - both Q tiles once, then the 8 K and
+//                8 V pages of every KV tile through the block table (2-D
+//                tensor maps over the pools viewed as [blocks*Hkv*16, D],
+//                128-byte swizzle) into a ring of K and V stages.
+//                warp 1: owns TMEM and issues every MMA from one thread:
+//                  S_i  = Q_i K_j^T   (SS: Q_i and K_j in smem)
+//                  O_i += P_i V_j     (TS: P_i in TMEM over S_i, V_j in smem)
+//                in the order S_0, S_1, PV_0, S_0', PV_1, S_1', ... so one
+//                tile's MMAs run while the other tile's softmax runs.
+//   warpgroups 1, 2  softmax of query tile 0 / 1, one thread per row (TMEM
+//                lane): S_i from TMEM, causal/prefix mask, online softmax in
+//                the log2 domain with lazy rescaling (O_i and l are rescaled
+//                only when the row max grows by more than 2^8), P_i packed to
+//                16-bit into S_i's TMEM columns, and finally O_i / l -> out.
 //
-// Every mbarrier wait is bounded; a timeout records FVB_ERR_DEVICE_TIMEOUT and
-// the CTA tears down (TMEM is always freed).
+// TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,256+D),
+// O_1 [384,384+D).  MMAs of one thread execute in issue order, so S_i of the
+// next KV tile (issued after PV_i) never overwrites P_i before PV_i read it,
+// and the commit that signals S_i also covers the preceding PV_i (the softmax
+// may then rescale O_i).  Every mbarrier wait is bounded; a timeout records
+// FVB_ERR_DEVICE_TIMEOUT and the CTA still frees its TMEM.
 #include <algorithm>
 
 #include "common.cuh"
@@ -40,33 +43,33 @@
 namespace fvb {
 namespace {
 
-constexpr int kTileM = 128;                      // rows: query tokens x GQA heads
-constexpr int kTileN = 128;                      // keys per KV tile
-constexpr int kThreads = 192;                    // 6 warps
-constexpr int kSoftmaxThreads = 128;
-constexpr int kHalfBytes = 128 * 128;            // 128 rows x one 128-byte swizzle span
+constexpr int kTileM = 128;            // rows per query tile: query tokens x GQA heads
+constexpr int kTileN = 128;            // keys per KV tile
+constexpr int kThreads = 384;          // 3 warpgroups
+constexpr int kWgThreads = 128;
+constexpr int kHalfBytes = 128 * 128;  // 128 rows x one 128-byte swizzle span
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.0f;   // lazy-rescale threshold (P <= 2^8)
+constexpr int kSortMaxSeqs = 2048;
 
 template <int D>
 struct Cfg {
-  static constexpr int kHalves = D / 64;         // 128-byte spans per row of Q / K / V
+  static constexpr int kHalves = D / 64;  // 128-byte spans per row of Q / K / V
   static constexpr int kStages = D == 128 ? 2 : 3;
-  static constexpr int kQBytes = kHalves * kHalfBytes;
+  static constexpr int kQTileBytes = kHalves * kHalfBytes;
   static constexpr int kKVBytes = kHalves * kHalfBytes;  // 128 keys of K (or V)
-  static constexpr int kPBytes = 2 * kHalfBytes;         // 128 rows x 128 keys
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffQ = 0;                        // two query tiles
+  static constexpr int kOffK = 2 * kQTileBytes;
   static constexpr int kOffV = kOffK + kStages * kKVBytes;
-  static constexpr int kOffP = kOffV + kStages * kKVBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_empty[2], p_full, o_done
-  static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 1 + 1;
+  static constexpr int kOffBar = kOffV + kStages * kKVBytes;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done[2]
+  static constexpr int kNumBars = 1 + 4 * kStages + 6;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColS = 0;
-  static constexpr uint32_t kColO = 256;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
+__device__ __forceinline__ uint32_t col_s(int i) { return uint32_t(i) * 128u; }
+__device__ __forceinline__ uint32_t col_o(int i) { return 256u + uint32_t(i) * 128u; }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -88,23 +91,49 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return __all_sync(0xffffffffu, ok);
 }
 
-// Exclusive scan of ceil(q_len / tile_tokens) over the sequences -> cu_tiles[0..num_seqs].
-__global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __restrict__ cu_seqlens, int num_seqs,
-                                                            int tile_tokens, int32_t* __restrict__ cu_tiles) {
+// Work plan of one launch (one CTA):
+//  order[p]    = p-th sequence by descending kv_len (identity beyond kSortMaxSeqs
+//                sequences), so the longest-context work is dispatched first;
+//  cu_items[p] = exclusive scan of ceil(ceil(q_len / tile_tokens) / 2) (query-tile
+//                pairs) over that order.
+__global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __restrict__ cu_seqlens,
+                                                            const int32_t* __restrict__ kv_lens, int num_seqs,
+                                                            int tile_tokens, int32_t* __restrict__ order,
+                                                            int32_t* __restrict__ cu_items) {
+  __shared__ int kv_sh[kSortMaxSeqs];
   __shared__ int warp_tot[32];
   __shared__ int carry;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const bool sort = num_seqs <= kSortMaxSeqs;
+  if (sort) {
+    for (int t = threadIdx.x; t < num_seqs; t += blockDim.x) kv_sh[t] = __ldg(kv_lens + t);
+  }
   if (threadIdx.x == 0) {
     carry = 0;
-    cu_tiles[0] = 0;
+    cu_items[0] = 0;
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < num_seqs; s += blockDim.x) {
+    int rank = s;
+    if (sort) {
+      const int ks = kv_sh[s];
+      rank = 0;
+      for (int t = 0; t < num_seqs; ++t) {
+        const int kt = kv_sh[t];
+        rank += (kt > ks) || (kt == ks && t < s);
+      }
+    }
+    order[rank] = s;
   }
   __syncthreads();
   for (int base = 0; base < num_seqs; base += blockDim.x) {
-    const int s = base + threadIdx.x;
+    const int p = base + threadIdx.x;
     int v = 0;
-    if (s < num_seqs) {
+    if (p < num_seqs) {
+      const int s = order[p];
       const int ql = __ldg(cu_seqlens + s + 1) - __ldg(cu_seqlens + s);
-      v = ql > 0 ? (ql + tile_tokens - 1) / tile_tokens : 0;
+      const int tiles = ql > 0 ? (ql + tile_tokens - 1) / tile_tokens : 0;
+      v = (tiles + 1) / 2;
     }
     int x = v;
 #pragma unroll
@@ -125,7 +154,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __res
     }
     __syncthreads();
     const int incl = x + (warp > 0 ? warp_tot[warp - 1] : 0) + carry;
-    if (s < num_seqs) cu_tiles[s + 1] = incl;
+    if (p < num_seqs) cu_items[p + 1] = incl;
     __syncthreads();
     if (threadIdx.x == blockDim.x - 1) carry = incl;
     __syncthreads();
@@ -136,9 +165,9 @@ template <typename T, int D, int NREP>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
     const __grid_constant__ CUtensorMap vmap, T* __restrict__ out, int64_t q_len_flatten, int num_seqs,
-    int n_kv_heads, int64_t num_blocks, const int32_t* __restrict__ cu_seqlens, const int32_t* __restrict__ cu_tiles,
-    const int32_t* __restrict__ block_tables, int max_blocks_per_seq, const int32_t* __restrict__ kv_lens,
-    const int32_t* __restrict__ positions, int* __restrict__ err) {
+    int n_kv_heads, int64_t num_blocks, const int32_t* __restrict__ cu_seqlens, const int32_t* __restrict__ order,
+    const int32_t* __restrict__ cu_items, const int32_t* __restrict__ block_tables, int max_blocks_per_seq,
+    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, int* __restrict__ err) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;  // query tokens per tile
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -150,43 +179,56 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   uint64_t* k_empty = k_full + C::kStages;
   uint64_t* v_full = k_empty + C::kStages;
   uint64_t* v_empty = v_full + C::kStages;
-  uint64_t* s_full = v_empty + C::kStages;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* o_done = p_full + 1;
+  uint64_t* s_full = v_empty + C::kStages;  // [2]
+  uint64_t* p_full = s_full + 2;            // [2]
+  uint64_t* o_done = p_full + 2;            // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
 
-  // ---- work item ----
-  const int tile_id = blockIdx.x, kvh = blockIdx.y;
-  if (tile_id >= __ldg(cu_tiles + num_seqs)) return;
+  // ---- work item: (query-tile pair, kv head); the heaviest items have the lowest ids ----
+  const int item = int(blockIdx.x) / n_kv_heads, kvh = int(blockIdx.x) % n_kv_heads;
+  if (item >= __ldg(cu_items + num_seqs)) return;
   int lo = 0, hi = num_seqs - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (__ldg(cu_tiles + mid) <= tile_id) lo = mid; else hi = mid - 1;
+    if (__ldg(cu_items + mid) <= item) lo = mid; else hi = mid - 1;
   }
-  const int s = lo;
-  const int tile = tile_id - __ldg(cu_tiles + s);
-  const int q_end = __ldg(cu_seqlens + s + 1);
-  const int t0 = __ldg(cu_seqlens + s) + tile * TOK;
-  const int t_last = min(t0 + TOK, q_end) - 1;
+  const int s = __ldg(order + lo);
+  const int q_begin = __ldg(cu_seqlens + s), q_end = __ldg(cu_seqlens + s + 1);
+  const int ntq = (q_end - q_begin + TOK - 1) / TOK;
+  const int pair = (ntq + 1) / 2 - 1 - (item - __ldg(cu_items + lo));  // last (longest-context) pair first
+  const bool has1 = 2 * pair + 1 < ntq;
   int kv_len = __ldg(kv_lens + s);
   if (kv_len > max_blocks_per_seq * kPageSize) {
     if (threadIdx.x == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, s);
     kv_len = max_blocks_per_seq * kPageSize;
   }
-  const int pos_last = min(__ldg(positions + t_last), kv_len - 1);
-  const int n_tiles = pos_last >= 0 ? pos_last / kTileN + 1 : 0;
-  const int need_pages = pos_last / kPageSize + 1;  // pages holding keys 0 .. pos_last
+  int t0[2], t_last[2], p_last[2], nkv[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    t0[i] = q_begin + (2 * pair + i) * TOK;
+    t_last[i] = min(t0[i] + TOK, q_end) - 1;
+    const bool live = i == 0 || has1;
+    p_last[i] = (live && kv_len > 0) ? max(min(__ldg(positions + t_last[i]), kv_len - 1), 0) : -1;
+    nkv[i] = p_last[i] >= 0 ? p_last[i] / kTileN + 1 : 0;
+  }
+  const int n_kv = max(nkv[0], nkv[1]);
+  const int need_pages = max(p_last[0], p_last[1]) / kPageSize + 1;  // pages holding every visible key
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (n_tiles == 0) {  // empty context (never produced by the engine): zeros, not garbage
-    for (int e = threadIdx.x; e < kTileM * D; e += kThreads) {
-      const int r = e / D, tok = t0 + r % TOK;
-      if (tok < q_end) out[(int64_t(kvh * NREP + r / TOK) * q_len_flatten + tok) * D + e % D] = Elem<T>::from_f(0.f);
+  if (n_kv == 0) {  // empty context (never produced by the engine): zeros, not garbage
+    for (int e = threadIdx.x; e < 2 * kTileM * D; e += kThreads) {
+      const int i = e / (kTileM * D), r = (e / D) % kTileM, tok = t0[i] + r % TOK;
+      if ((i == 0 || has1) && tok <= t_last[i])
+        out[(int64_t(kvh * NREP + r / TOK) * q_len_flatten + tok) * D + e % D] = Elem<T>::from_f(0.f);
     }
     return;
   }
 
+  // V rows that no TMA writes before a PV reads them must hold finite data.
+  for (int e = threadIdx.x; e < C::kStages * C::kKVBytes / 16; e += kThreads) {
+    sts_v4(smem_u32(smem + C::kOffV) + e * 16, make_uint4(0, 0, 0, 0));
+  }
+  fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < C::kStages; ++i) {
@@ -197,10 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kSoftmaxThreads);
+      mbar_init(&p_full[i], kWgThreads);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, kSoftmaxThreads);
-    mbar_init(o_done, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -211,28 +252,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t sm_q = smem_u32(smem + C::kOffQ);
-  const uint32_t sm_k = smem_u32(smem + C::kOffK);
-  const uint32_t sm_v = smem_u32(smem + C::kOffV);
-  const uint32_t sm_p = smem_u32(smem + C::kOffP);
+  const int wg = threadIdx.x / kWgThreads;
 
-  if (warp == 0) {
-    // ============================ TMA producer ============================
-    if (lane == 0) {
+  if (wg == 0) {
+    if (warp == 0 && lane == 0) {
+      // ============================ TMA producer ============================
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      mbar_arrive_expect_tx(q_full, C::kQBytes);
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * C::kQTileBytes);
+      for (int i = 0; i < (has1 ? 2 : 1); ++i) {
 #pragma unroll
-      for (int g = 0; g < NREP; ++g) {
-        const int row = int((int64_t(kvh) * NREP + g) * q_len_flatten + t0);
+        for (int g = 0; g < NREP; ++g) {
+          const int row = int((int64_t(kvh) * NREP + g) * q_len_flatten + t0[i]);
 #pragma unroll
-        for (int h = 0; h < C::kHalves; ++h) {
-          tma_load_2d(smem + C::kOffQ + h * kHalfBytes + g * TOK * 128, &qmap, h * 64, row, q_full);
+          for (int h = 0; h < C::kHalves; ++h) {
+            tma_load_2d(smem + C::kOffQ + i * C::kQTileBytes + h * kHalfBytes + g * TOK * 128, &qmap, h * 64, row,
+                        q_full);
+          }
         }
       }
       const int32_t* table = block_tables + int64_t(s) * max_blocks_per_seq;
-      for (int j = 0; j < n_tiles; ++j) {
+      for (int j = 0; j < n_kv; ++j) {
         const int st = j % C::kStages, use = j / C::kStages;
         const int p0 = j * (kTileN / kPageSize);
         const int np = min(kTileN / kPageSize, need_pages - p0);
@@ -265,148 +306,183 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
           }
         }
       }
-    }
-  } else if (warp == 1) {
-    // ============================ MMA issuer ============================
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      // ============================ MMA issuer ============================
       constexpr uint32_t idesc_s = umma_idesc_f16(kBF16, kTileM, kTileN, false);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBF16, kTileM, D, true);
-      bool ok = mbar_wait(q_full, 0, err, 0x310);
-      for (int j = 0; ok && j <= n_tiles; ++j) {
-        if (j < n_tiles) {
-          const int st = j % C::kStages, sb = j & 1;
-          ok = mbar_wait(&k_full[st], (j / C::kStages) & 1, err, 0x311);
-          if (ok && j >= 2) ok = mbar_wait(&s_empty[sb], ((j >> 1) - 1) & 1, err, 0x312);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t kst = sm_k + st * C::kKVBytes;
+      const uint32_t sm_q = smem_u32(smem + C::kOffQ);
+      const uint32_t sm_k = smem_u32(smem + C::kOffK);
+      const uint32_t sm_v = smem_u32(smem + C::kOffV);
+      auto issue_s = [&](int i, int st) {
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-            umma_f16_ss(tmem + C::kColS + sb * kTileN, umma_sdesc_sw128(sm_q + off, 16, 1024),
-                        umma_sdesc_sw128(kst + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[sb]);
-          umma_commit(&k_empty[st]);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          umma_f16_ss(tmem + col_s(i), umma_sdesc_sw128(sm_q + i * C::kQTileBytes + off, 16, 1024),
+                      umma_sdesc_sw128(sm_k + st * C::kKVBytes + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        if (j >= 1) {
-          const int jj = j - 1, st = jj % C::kStages;
-          ok = mbar_wait(p_full, jj & 1, err, 0x313);
-          if (ok) ok = mbar_wait(&v_full[st], (jj / C::kStages) & 1, err, 0x314);
+      };
+      auto issue_pv = [&](int i, int st, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < kTileN / 16; ++kk) {
+          umma_f16_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8,
+                      umma_sdesc_sw128(sm_v + st * C::kKVBytes + kk * 16 * 128, kHalfBytes, 1024), idesc_o,
+                      (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, err, 0x310) && mbar_wait(&k_full[0], 0, err, 0x311);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        umma_commit(&s_full[0]);
+        if (has1) {
+          issue_s(1, 0);
+          umma_commit(&s_full[1]);
+        }
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % C::kStages, nst = (j + 1) % C::kStages;
+        const uint32_t vph = (j / C::kStages) & 1, nkph = ((j + 1) / C::kStages) & 1;
+        bool k_next = false;
+        if (j < nkv[0]) {
+          ok = mbar_wait(&p_full[0], j & 1, err, 0x312) && mbar_wait(&v_full[st], vph, err, 0x313);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t vst = sm_v + st * C::kKVBytes;
-#pragma unroll
-          for (int kk = 0; kk < kTileN / 16; ++kk) {
-            umma_f16_ss(tmem + C::kColO, umma_sdesc_sw128(sm_p + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024),
-                        umma_sdesc_sw128(vst + kk * 16 * 128, kHalfBytes, 1024), idesc_o,
-                        (jj > 0 || kk > 0) ? 1u : 0u);
+          issue_pv(0, st, j > 0);
+          if (j == nkv[0] - 1) umma_commit(&o_done[0]);
+          if (j + 1 < nkv[0]) {
+            ok = mbar_wait(&k_full[nst], nkph, err, 0x314);
+            if (!ok) break;
+            k_next = true;
+            tc_fence_after();
+            issue_s(0, nst);
+            umma_commit(&s_full[0]);
           }
-          umma_commit(o_done);
+          if (!has1) {
+            umma_commit(&v_empty[st]);
+            if (j + 1 < nkv[0]) umma_commit(&k_empty[nst]);
+          }
+        }
+        if (has1 && j < nkv[1]) {
+          ok = mbar_wait(&p_full[1], j & 1, err, 0x315) && mbar_wait(&v_full[st], vph, err, 0x316);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(1, st, j > 0);
+          if (j == nkv[1] - 1) umma_commit(&o_done[1]);
           umma_commit(&v_empty[st]);
+          if (j + 1 < nkv[1]) {
+            if (!k_next) {
+              ok = mbar_wait(&k_full[nst], nkph, err, 0x317);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_s(1, nst);
+            umma_commit(&s_full[1]);
+            umma_commit(&k_empty[nst]);
+          }
         }
       }
     }
-  } else {
-    // ============================ softmax / epilogue ============================
+  } else if (wg - 1 == 0 || has1) {
+    // ============================ softmax / epilogue of query tile i ============================
+    const int i = wg - 1;
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;  // tile row == TMEM lane
-    const int g = r / TOK, tok = t0 + r % TOK;
-    const bool row_valid = tok <= t_last;
+    const int g = r / TOK, tok = t0[i] + r % TOK;
+    const bool row_valid = tok <= t_last[i];
     const int head = kvh * NREP + g;
-    int pos = row_valid ? __ldg(positions + tok) : pos_last;
+    int pos = row_valid ? __ldg(positions + tok) : p_last[i];
     pos = max(min(pos, kv_len - 1), 0);
     const float scale = kLog2e * rsqrtf(float(D));
+    const float2 scale2 = make_float2(scale, scale);
     const uint32_t t_row = tmem + (uint32_t(q4 * 32) << 16);
-    float m = -INFINITY, l = 0.f;
+    float m_ref = -INFINITY;  // raw-score reference max of P and l
+    float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      ok = warp_wait(&s_full[sb], (j >> 1) & 1, err, 0x320);
+    for (int j = 0; j < nkv[i]; ++j) {
+      ok = warp_wait(&s_full[i], j & 1, err, 0x320 + i);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_ld_32cols(t_row + C::kColS + sb * kTileN + c4 * 32, sr[c4]);
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
-
+      uint32_t sr[128];
+      tmem_ld_128cols(t_row + col_s(i), sr);
       const int kbase = j * kTileN;
-      const bool masked = kbase + kTileN - 1 > pos;
-      float mt = -INFINITY;
+      if (kbase + kTileN - 1 > pos) {
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          float x = __uint_as_float(sr[c4][c]);
-          if (masked && kbase + c4 * 32 + c > pos) x = -INFINITY;
-          sr[c4][c] = __float_as_uint(x);
-          mt = fmaxf(mt, x);
+        for (int c = 0; c < 128; ++c) {
+          if (kbase + c > pos) sr[c] = __float_as_uint(-INFINITY);
         }
       }
-      const float m_new = fmaxf(m, mt);  // finite: key 0 is visible to every row in tile 0
-      const float ms = m_new * scale;
-      const float corr = fast_exp2((m - m_new) * scale);
-      float rs = 0.f;
+      float mx[8];
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int a = 0; a < 8; ++a) mx[a] = __uint_as_float(sr[a]);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p = fast_exp2(fmaf(__uint_as_float(sr[c4][c]), scale, -ms));
-          rs += p;
-          sr[c4][c] = __float_as_uint(p);
-        }
-      }
-      l = l * corr + rs;
-      if (j > 0) {
-        // PV_{j-1} must be done before O is rescaled and the P tile overwritten.
-        ok = warp_wait(o_done, (j - 1) & 1, err, 0x321);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, m_new > m)) {
+      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sr[c]));
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      if (j == 0) {
+        m_ref = mt;  // finite: key 0 is visible to every row
+      } else {
+        const bool grow = (mt - m_ref) * scale > kRescaleLog2;
+        if (__any_sync(0xffffffffu, grow)) {
+          // O_i holds P V over earlier tiles relative to m_ref: rescale rows whose max grew.
+          const float corr = grow ? fast_exp2((m_ref - mt) * scale) : 1.f;
+          const float2 corr2 = make_float2(corr, corr);
+          if (grow) {
+            l *= corr;
+            m_ref = mt;
+          }
 #pragma unroll 1
           for (int cc = 0; cc < D / 32; ++cc) {
             uint32_t o[32];
-            tmem_ld_32cols(t_row + C::kColO + cc * 32, o);
+            tmem_ld_32cols(t_row + col_o(i) + cc * 32, o);
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * corr);
-            tmem_st_32cols(t_row + C::kColO + cc * 32, o);
+            for (int c = 0; c < 32; c += 2) {
+              float2 v = __fmul2_rn(make_float2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])), corr2);
+              o[c] = __float_as_uint(v.x);
+              o[c + 1] = __float_as_uint(v.y);
+            }
+            tmem_st_32cols(t_row + col_o(i) + cc * 32, o);
           }
-          tmem_wait_st();
         }
       }
-      m = m_new;
-      // P row (K-major, 128-byte swizzle: 16-byte chunk c of row r at c ^ (r % 8))
+      // P = 2^((s - m_ref) * scale) <= 2^8, packed to 16 bits into S_i's first 64 columns.
+      const float ms = m_ref * scale;
+      const float2 nms2 = make_float2(-ms, -ms);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      uint32_t pk[64];
 #pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        const uint32_t* src = &sr[cc >> 2][(cc & 3) * 8];
-        uint4 v;
-        v.x = pack2<T>(__uint_as_float(src[0]), __uint_as_float(src[1]));
-        v.y = pack2<T>(__uint_as_float(src[2]), __uint_as_float(src[3]));
-        v.z = pack2<T>(__uint_as_float(src[4]), __uint_as_float(src[5]));
-        v.w = pack2<T>(__uint_as_float(src[6]), __uint_as_float(src[7]));
-        sts_v4(sm_p + (cc >> 3) * kHalfBytes + r * 128 + (((cc & 7) ^ (r & 7)) << 4), v);
+      for (int c = 0; c < 128; c += 2) {
+        const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), scale2, nms2);
+        const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        acc[(c >> 1) & 3] = __fadd2_rn(acc[(c >> 1) & 3], p);
+        pk[c >> 1] = pack2<T>(p.x, p.y);
       }
-      if (j == n_tiles - 1 && kbase + kTileN - 1 > pos_last) {
-        // Keys past pos_last are masked for every row (P = 0), but their V rows are
-        // unloaded or uninitialised pool slots: zero them so 0 * NaN cannot occur.
+      const float2 a01 = __fadd2_rn(acc[0], acc[1]), a23 = __fadd2_rn(acc[2], acc[3]);
+      const float2 a = __fadd2_rn(a01, a23);
+      l += a.x + a.y;
+      tmem_st_64cols(t_row + col_s(i), pk);
+      tmem_wait_st();
+      if (j == nkv[i] - 1 && kbase + kTileN > kv_len) {
+        // Keys >= kv_len in the last KV tile were loaded from uninitialised pool
+        // slots; P is 0 there, but 0 * NaN is not, so zero those V rows.
         const int st = j % C::kStages;
-        ok = warp_wait(&v_full[st], (j / C::kStages) & 1, err, 0x322);
+        ok = warp_wait(&v_full[st], (j / C::kStages) & 1, err, 0x324 + i);
         if (!ok) break;
-        if (kbase + r > pos_last) {
+        if (kbase + r >= kv_len) {
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h) {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) sts_v4(sm_v + st * C::kKVBytes + h * kHalfBytes + r * 128 + c * 16,
-                                               make_uint4(0, 0, 0, 0));
+            for (int c = 0; c < 8; ++c)
+              sts_v4(smem_u32(smem + C::kOffV + st * C::kKVBytes + h * kHalfBytes + r * 128 + c * 16),
+                     make_uint4(0, 0, 0, 0));
           }
         }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[i]);
     }
-    if (ok) ok = warp_wait(o_done, (n_tiles - 1) & 1, err, 0x323);
+    if (ok) ok = warp_wait(&o_done[i], 0, err, 0x326 + i);
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.f / l;
@@ -414,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t o[32];
-        tmem_ld_32cols(t_row + C::kColO + cc * 32, o);
+        tmem_ld_32cols(t_row + col_o(i) + cc * 32, o);
         if (row_valid) {
           uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
@@ -455,16 +531,19 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   if (ce == cudaSuccess) ce = make_tma_2d(&kmap, k_pool, tdt, D, pool_rows, D * 2, 64, kPageSize, true);
   if (ce == cudaSuccess) ce = make_tma_2d(&vmap, v_pool, tdt, D, pool_rows, D * 2, 64, kPageSize, true);
   if (ce != cudaSuccess) return ce;
-  int32_t* cu_tiles = static_cast<int32_t*>(workspace);
-  prefill_plan_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, num_seqs, TOK, cu_tiles);
+  int32_t* order = static_cast<int32_t*>(workspace);
+  int32_t* cu_items = order + ((num_seqs + 63) & ~63);
+  prefill_plan_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, kv_lens, num_seqs, TOK, order, cu_items);
   ce = cudaGetLastError();
   if (ce != cudaSuccess) return ce;
   auto kern = prefill_tc_kernel<T, D, NREP>;
   ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (ce != cudaSuccess) return ce;
-  dim3 grid(unsigned(plan.max_tiles), unsigned(n_kv_heads));
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(qmap, kmap, vmap, static_cast<T*>(out), q_len_flatten, num_seqs,
-                                                  n_kv_heads, num_blocks, cu_seqlens, cu_tiles, block_tables,
+  const int64_t ctas = plan.max_tiles * n_kv_heads;
+  if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
+  kern<<<unsigned(ctas), kThreads, C::kSmemBytes, stream>>>(qmap, kmap, vmap, static_cast<T*>(out), q_len_flatten,
+                                                            num_seqs, n_kv_heads, num_blocks, cu_seqlens, order,
+                                                            cu_items, block_tables,
                                                   max_blocks_per_seq, kv_lens, positions, err);
   return cudaGetLastError();
 }
@@ -506,9 +585,10 @@ PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim
     return p;
   }
   p.tile_tokens = kTileM / (n_heads / n_kv_heads);
-  // Each sequence wastes at most one partial tile.
-  p.max_tiles = (q_len_flatten + p.tile_tokens - 1) / p.tile_tokens + num_seqs;
-  p.ws_bytes = ((size_t(num_seqs) + 1) * 4 + 255) & ~size_t(255);
+  // Work items are query-tile pairs; each sequence wastes at most one partial pair.
+  p.max_tiles = (q_len_flatten + 2 * p.tile_tokens - 1) / (2 * p.tile_tokens) + num_seqs;
+  // order[num_seqs] (padded to 64 entries) + cu_items[num_seqs + 1]
+  p.ws_bytes = ((size_t((num_seqs + 63) & ~63) + num_seqs + 1) * 4 + 255) & ~size_t(255);
   return p;
 }
 
