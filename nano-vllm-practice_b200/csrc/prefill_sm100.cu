@@ -55,15 +55,18 @@ constexpr int kSortMaxSeqs = 2048;
 template <int D>
 struct Cfg {
   static constexpr int kHalves = D / 64;  // 128-byte spans per row of Q / K / V
-  static constexpr int kStages = D == 128 ? 2 : 3;
+  // K and V rings are separate: K is needed one MMA slot earlier than V, so
+  // it gets the deeper ring when shared memory is short (D = 128).
+  static constexpr int kKStages = D == 128 ? 3 : 4;
+  static constexpr int kVStages = D == 128 ? 2 : 4;
   static constexpr int kQTileBytes = kHalves * kHalfBytes;
   static constexpr int kKVBytes = kHalves * kHalfBytes;  // 128 keys of K (or V)
   static constexpr int kOffQ = 0;                        // two query tiles
   static constexpr int kOffK = 2 * kQTileBytes;
-  static constexpr int kOffV = kOffK + kStages * kKVBytes;
-  static constexpr int kOffBar = kOffV + kStages * kKVBytes;
+  static constexpr int kOffV = kOffK + kKStages * kKVBytes;
+  static constexpr int kOffBar = kOffV + kVStages * kKVBytes;
   // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done[2]
-  static constexpr int kNumBars = 1 + 4 * kStages + 6;
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 6;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -176,10 +179,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + C::kStages;
-  uint64_t* v_full = k_empty + C::kStages;
-  uint64_t* v_empty = v_full + C::kStages;
-  uint64_t* s_full = v_empty + C::kStages;  // [2]
+  uint64_t* k_empty = k_full + C::kKStages;
+  uint64_t* v_full = k_empty + C::kKStages;
+  uint64_t* v_empty = v_full + C::kVStages;
+  uint64_t* s_full = v_empty + C::kVStages;  // [2]
   uint64_t* p_full = s_full + 2;            // [2]
   uint64_t* o_done = p_full + 2;            // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
@@ -225,15 +228,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   }
 
   // V rows that no TMA writes before a PV reads them must hold finite data.
-  for (int e = threadIdx.x; e < C::kStages * C::kKVBytes / 16; e += kThreads) {
+  for (int e = threadIdx.x; e < C::kVStages * C::kKVBytes / 16; e += kThreads) {
     sts_v4(smem_u32(smem + C::kOffV) + e * 16, make_uint4(0, 0, 0, 0));
   }
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < C::kStages; ++i) {
+    for (int i = 0; i < C::kKStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < C::kVStages; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
@@ -255,29 +260,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   const int wg = threadIdx.x / kWgThreads;
 
   if (wg == 0) {
-    if (warp == 0 && lane == 0) {
-      // ============================ TMA producer ============================
-      prefetch_tensormap(&qmap);
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
-      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * C::kQTileBytes);
-      for (int i = 0; i < (has1 ? 2 : 1); ++i) {
+    if ((warp == 0 || warp == 2) && lane == 0) {
+      // ======================= TMA producers: warp 0 = Q + K, warp 2 = V =======================
+      const bool is_k = warp == 0;
+      prefetch_tensormap(is_k ? &kmap : &vmap);
+      if (is_k) {
+        prefetch_tensormap(&qmap);
+        mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * C::kQTileBytes);
+        for (int i = 0; i < (has1 ? 2 : 1); ++i) {
 #pragma unroll
-        for (int g = 0; g < NREP; ++g) {
-          const int row = int((int64_t(kvh) * NREP + g) * q_len_flatten + t0[i]);
+          for (int g = 0; g < NREP; ++g) {
+            const int row = int((int64_t(kvh) * NREP + g) * q_len_flatten + t0[i]);
 #pragma unroll
-          for (int h = 0; h < C::kHalves; ++h) {
-            tma_load_2d(smem + C::kOffQ + i * C::kQTileBytes + h * kHalfBytes + g * TOK * 128, &qmap, h * 64, row,
-                        q_full);
+            for (int h = 0; h < C::kHalves; ++h) {
+              tma_load_2d(smem + C::kOffQ + i * C::kQTileBytes + h * kHalfBytes + g * TOK * 128, &qmap, h * 64, row,
+                          q_full);
+            }
           }
         }
       }
+      const int nst_ring = is_k ? C::kKStages : C::kVStages;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint8_t* ring = smem + (is_k ? C::kOffK : C::kOffV);
+      const CUtensorMap* map = is_k ? &kmap : &vmap;
       const int32_t* table = block_tables + int64_t(s) * max_blocks_per_seq;
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::kStages, use = j / C::kStages;
+        const int st = j % nst_ring, use = j / nst_ring;
         const int p0 = j * (kTileN / kPageSize);
         const int np = min(kTileN / kPageSize, need_pages - p0);
-        const uint32_t bytes = uint32_t(np) * kPageSize * D * 2;
         int rows[kTileN / kPageSize];
         for (int pi = 0; pi < np; ++pi) {
           int blk = __ldg(table + p0 + pi);
@@ -287,22 +298,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
           }
           rows[pi] = (blk * n_kv_heads + kvh) * kPageSize;
         }
-        if (use > 0 && !mbar_wait(&k_empty[st], (use - 1) & 1, err, 0x300)) break;
-        mbar_arrive_expect_tx(&k_full[st], bytes);
+        if (use > 0 && !mbar_wait(&empty[st], (use - 1) & 1, err, is_k ? 0x300 : 0x301)) break;
+        mbar_arrive_expect_tx(&full[st], uint32_t(np) * kPageSize * D * 2);
         for (int pi = 0; pi < np; ++pi) {
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h) {
-            tma_load_2d(smem + C::kOffK + st * C::kKVBytes + h * kHalfBytes + pi * kPageSize * 128, &kmap, h * 64,
-                        rows[pi], &k_full[st]);
-          }
-        }
-        if (use > 0 && !mbar_wait(&v_empty[st], (use - 1) & 1, err, 0x301)) break;
-        mbar_arrive_expect_tx(&v_full[st], bytes);
-        for (int pi = 0; pi < np; ++pi) {
-#pragma unroll
-          for (int h = 0; h < C::kHalves; ++h) {
-            tma_load_2d(smem + C::kOffV + st * C::kKVBytes + h * kHalfBytes + pi * kPageSize * 128, &vmap, h * 64,
-                        rows[pi], &v_full[st]);
+            tma_load_2d(ring + st * C::kKVBytes + h * kHalfBytes + pi * kPageSize * 128, map, h * 64, rows[pi],
+                        &full[st]);
           }
         }
       }
@@ -341,8 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
         umma_commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % C::kStages, nst = (j + 1) % C::kStages;
-        const uint32_t vph = (j / C::kStages) & 1, nkph = ((j + 1) / C::kStages) & 1;
+        const int st = j % C::kVStages, nst = (j + 1) % C::kKStages;
+        const uint32_t vph = (j / C::kVStages) & 1, nkph = ((j + 1) / C::kKStages) & 1;
         bool k_next = false;
         if (j < nkv[0]) {
           ok = mbar_wait(&p_full[0], j & 1, err, 0x312) && mbar_wait(&v_full[st], vph, err, 0x313);
@@ -383,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
         }
       }
     }
-  } else if (wg - 1 == 0 || has1) {
+  } else if (wg == 1 || has1) {
     // ============================ softmax / epilogue of query tile i ============================
     const int i = wg - 1;
     const int q4 = warp & 3;
@@ -465,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       if (j == nkv[i] - 1 && kbase + kTileN > kv_len) {
         // Keys >= kv_len in the last KV tile were loaded from uninitialised pool
         // slots; P is 0 there, but 0 * NaN is not, so zero those V rows.
-        const int st = j % C::kStages;
-        ok = warp_wait(&v_full[st], (j / C::kStages) & 1, err, 0x324 + i);
+        const int st = j % C::kVStages;
+        ok = warp_wait(&v_full[st], (j / C::kVStages) & 1, err, 0x324 + i);
         if (!ok) break;
         if (kbase + r >= kv_len) {
 #pragma unroll
