@@ -315,19 +315,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       const uint32_t sm_q = smem_u32(smem + C::kOffQ);
       const uint32_t sm_k = smem_u32(smem + C::kOffK);
       const uint32_t sm_v = smem_u32(smem + C::kOffV);
+      // Descriptors are built once; an operand at byte offset `off` from a base is
+      // base descriptor + off / 16 (shared-memory addresses stay below 256 KB, so
+      // the 14-bit start-address field never carries).
+      const uint64_t dq = umma_sdesc_sw128(sm_q, 16, 1024);
+      const uint64_t dk = umma_sdesc_sw128(sm_k, 16, 1024);
+      const uint64_t dv = umma_sdesc_sw128(sm_v, kHalfBytes, 1024);
       auto issue_s = [&](int i, int st) {
+        const uint64_t qd = dq + uint64_t((i * C::kQTileBytes) >> 4);
+        const uint64_t kd = dk + uint64_t((st * C::kKVBytes) >> 4);
+        const uint32_t d_tmem = tmem + col_s(i);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16_ss(tmem + col_s(i), umma_sdesc_sw128(sm_q + i * C::kQTileBytes + off, 16, 1024),
-                      umma_sdesc_sw128(sm_k + st * C::kKVBytes + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          const uint64_t off = uint64_t(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
+          umma_f16_ss(d_tmem, qd + off, kd + off, idesc_s, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int i, int st, bool acc) {
+        const uint64_t vd = dv + uint64_t((st * C::kKVBytes) >> 4);
+        const uint32_t d_tmem = tmem + col_o(i), a_tmem = tmem + col_s(i);
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk) {
-          umma_f16_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8,
-                      umma_sdesc_sw128(sm_v + st * C::kKVBytes + kk * 16 * 128, kHalfBytes, 1024), idesc_o,
+          umma_f16_ts(d_tmem, a_tmem + kk * 8, vd + uint64_t((kk * 16 * 128) >> 4), idesc_o,
                       (acc || kk > 0) ? 1u : 0u);
         }
       };

@@ -91,6 +91,8 @@ class FvbError(RuntimeError):
 
 def check(status: int, what: str) -> None:
     if status != FVB_OK:
+        if status == 5 and _lib is not None:  # FVB_ERR_CUDA: name the runtime error
+            raise FvbError(status, f"{what} (cudaError {_lib.fvb_last_cuda_error()})")
         raise FvbError(status, what)
 
 
