@@ -74,6 +74,13 @@ struct Cfg {
 __device__ __forceinline__ uint32_t col_s(int i) { return uint32_t(i) * 128u; }
 __device__ __forceinline__ uint32_t col_o(int i) { return 256u + uint32_t(i) * 128u; }
 
+// max(a, b, c) in one instruction (3-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -215,7 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     nkv[i] = p_last[i] >= 0 ? p_last[i] / kTileN + 1 : 0;
   }
   const int n_kv = max(nkv[0], nkv[1]);
-  const int need_pages = max(p_last[0], p_last[1]) / kPageSize + 1;  // pages holding every visible key
+  const int pos_max = max(p_last[0], p_last[1]);  // last key visible to any row of the item
+  const int need_pages = pos_max / kPageSize + 1;  // pages holding every visible key
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (n_kv == 0) {  // empty context (never produced by the engine): zeros, not garbage
@@ -227,11 +235,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     return;
   }
 
-  // V rows that no TMA writes before a PV reads them must hold finite data.
-  for (int e = threadIdx.x; e < C::kVStages * C::kKVBytes / 16; e += kThreads) {
-    sts_v4(smem_u32(smem + C::kOffV) + e * 16, make_uint4(0, 0, 0, 0));
-  }
-  fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < C::kKStages; ++i) {
@@ -427,9 +430,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx[a] = __uint_as_float(sr[a]);
 #pragma unroll
-      for (int c = 8; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sr[c]));
-      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int c = 8; c < 120; c += 16) {
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mx[a] = fmax3(mx[a], __uint_as_float(sr[c + a]), __uint_as_float(sr[c + 8 + a]));
+      }
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx[a] = fmaxf(mx[a], __uint_as_float(sr[120 + a]));
+      const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       if (j == 0) {
         m_ref = mt;  // finite: key 0 is visible to every row
       } else {
@@ -463,7 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 128; c += 2) {
-        const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), scale2, nms2);
+        const float2 x =
+            __ffma2_rn(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), scale2, nms2);
         const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         acc[(c >> 1) & 3] = __fadd2_rn(acc[(c >> 1) & 3], p);
         pk[c >> 1] = pack2<T>(p.x, p.y);
@@ -473,13 +481,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       l += a.x + a.y;
       tmem_st_64cols(t_row + col_s(i), pk);
       tmem_wait_st();
-      if (j == nkv[i] - 1 && kbase + kTileN > kv_len) {
-        // Keys >= kv_len in the last KV tile were loaded from uninitialised pool
-        // slots; P is 0 there, but 0 * NaN is not, so zero those V rows.
+      if (j == n_kv - 1 && kbase + kTileN - 1 > pos_max) {
+        // Keys past the last visible one (pos_max) in the final KV tile are either
+        // not loaded (stale shared memory) or uninitialised pool slots: P is 0
+        // there, but 0 * NaN is not, so zero those V rows before the PV reads them.
         const int st = j % C::kVStages;
         ok = warp_wait(&v_full[st], (j / C::kVStages) & 1, err, 0x324 + i);
         if (!ok) break;
-        if (kbase + r >= kv_len) {
+        if (kbase + r > pos_max) {
 #pragma unroll
           for (int h = 0; h < C::kHalves; ++h) {
 #pragma unroll
