@@ -56,7 +56,13 @@ class ClockSampler:
     )
 
     def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
+        # nvidia-smi numbers GPUs physically; address this process's device by UUID.
+        try:
+            import torch
+
+            self.gpu_index = f"GPU-{torch.cuda.get_device_properties(gpu_index).uuid}"
+        except Exception:
+            self.gpu_index = str(gpu_index)
         self.proc = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"fvb_clocks_{os.getpid()}.csv"
 
@@ -163,6 +169,18 @@ def time_cpu_baseline(sub, steps: int, warmup: int) -> tuple[float, float]:
         t.append(time.perf_counter() - t0)
     med = float(np.median(t))
     return sub["bytes"] / med / 1e9, med
+
+
+def _cpu_threads():
+    """Let numpy's BLAS use every host core (torchrun sets OMP_NUM_THREADS=1 for its workers)."""
+    try:
+        from threadpoolctl import threadpool_limits
+
+        return threadpool_limits(limits=os.cpu_count() or 1)
+    except Exception:
+        import contextlib
+
+        return contextlib.nullcontext()
 
 
 def _blas_threads() -> int:
@@ -283,8 +301,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         sub = cpu_decode_sample(batch, args.cpu_seqs)
-        gbs, med = time_cpu_baseline(sub, steps=3, warmup=1)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": _blas_threads(), "kind": "port",
+        with _cpu_threads():
+            gbs, med = time_cpu_baseline(sub, steps=3, warmup=1)
+            cores = _blas_threads()
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                "sample": f"{len(sub['kv_lens'])} of {batch.num_seqs} config-2 sequences (store + decode), "
                          f"fp32 numpy oracle, median of 3 steps ({med * 1e3:.1f} ms/step)"}
     return gathered, clocks, decode_bytes, launches_per_step, cpu, (h2d, d2h), batch
@@ -469,16 +489,17 @@ def run_reference_arm(args, rank: int, world: int):
     sub["k_new"] = small.k_new.float().numpy()
     sub["v_new"] = small.v_new.float().numpy()
     sub["bytes"] = _decode_step_bytes(small)
-    for _ in range(args.warmup):
-        cpu_decode_step(sub)
-    t = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        cpu_decode_step(sub)
-        t.append(time.perf_counter() - t0)
+    with _cpu_threads():
+        for _ in range(args.warmup):
+            cpu_decode_step(sub)
+        t = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            cpu_decode_step(sub)
+            t.append(time.perf_counter() - t0)
+        cores = _blas_threads()
     mean = float(np.mean(t))
     value = sub["bytes"] / mean / 1e9
-    cores = _blas_threads()
     sample = (f"{len(seqs)} of 256 config-2 sequences per step (store + decode, fp32 numpy restatement of "
               f"qwen3.py:240-264 + 430-542)")
     print(json.dumps({
