@@ -422,7 +422,8 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
     elif args.workload == "mixed":
         batch = workloads.config4(seed=4 + rank)
     else:
-        batch = workloads.config5(rank=rank, world=world)
+        total = args.num_seqs if args.num_seqs != 256 else 64  # config 5: 64 sequences over all ranks
+        batch = workloads.config5(rank=rank, world=world, total=total)
     batch.materialize(dev)
     md = batch.device_metadata(dev)
     stream = torch.cuda.current_stream()

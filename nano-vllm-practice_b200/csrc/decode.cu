@@ -225,10 +225,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     const uint32_t kslot = smem_base + Tr::kOffK + slot * Tr::kStageBytes;
     const uint32_t vslot = smem_base + Tr::kOffV + slot * Tr::kStageBytes;
 
-    // s[r] = q_r . k_lane  (log2 units)
-    float s[NREP];
+    // s[r] = q_r . k_lane  (log2 units).  Four independent fp32 partial sums per
+    // head (two packed fp32x2 accumulators) keep the FMA dependency chains short.
+    float2 sp[NREP][2];
 #pragma unroll
-    for (int r = 0; r < NREP; ++r) s[r] = 0.f;
+    for (int r = 0; r < NREP; ++r) sp[r][0] = sp[r][1] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < Tr::kChunks; ++c) {
       const uint32_t kaddr = kslot + k_lane_off + (c >> 3) * 2048 + ((((c & 7) ^ (kr & 7))) << 4);
@@ -239,13 +240,14 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
 #pragma unroll
         for (int e = 0; e < Tr::kVec; e += 4) {
           const float4 qv = *reinterpret_cast<const float4*>(qs + r * D + c * Tr::kVec + e);
-          s[r] = fmaf(qv.x, kf[e + 0], s[r]);
-          s[r] = fmaf(qv.y, kf[e + 1], s[r]);
-          s[r] = fmaf(qv.z, kf[e + 2], s[r]);
-          s[r] = fmaf(qv.w, kf[e + 3], s[r]);
+          sp[r][0] = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(kf[e + 0], kf[e + 1]), sp[r][0]);
+          sp[r][1] = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(kf[e + 2], kf[e + 3]), sp[r][1]);
         }
       }
     }
+    float s[NREP];
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) s[r] = (sp[r][0].x + sp[r][1].x) + (sp[r][0].y + sp[r][1].y);
     const bool valid = lane < nvalid;
 #pragma unroll
     for (int r = 0; r < NREP; ++r) {

@@ -437,30 +437,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx[a] = fmaxf(mx[a], __uint_as_float(sr[120 + a]));
       const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      // Lazy rescale: keep the reference max unless this tile's max exceeds it by
+      // more than 2^8; rows that grow rescale l now and O (in TMEM) after P is out.
+      float corr = 1.f;
+      bool rescale = false;
       if (j == 0) {
         m_ref = mt;  // finite: key 0 is visible to every row
       } else {
         const bool grow = (mt - m_ref) * scale > kRescaleLog2;
-        if (__any_sync(0xffffffffu, grow)) {
-          // O_i holds P V over earlier tiles relative to m_ref: rescale rows whose max grew.
-          const float corr = grow ? fast_exp2((m_ref - mt) * scale) : 1.f;
-          const float2 corr2 = make_float2(corr, corr);
-          if (grow) {
-            l *= corr;
-            m_ref = mt;
-          }
-#pragma unroll 1
-          for (int cc = 0; cc < D / 32; ++cc) {
-            uint32_t o[32];
-            tmem_ld_32cols(t_row + col_o(i) + cc * 32, o);
-#pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-              float2 v = __fmul2_rn(make_float2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])), corr2);
-              o[c] = __float_as_uint(v.x);
-              o[c + 1] = __float_as_uint(v.y);
-            }
-            tmem_st_32cols(t_row + col_o(i) + cc * 32, o);
-          }
+        rescale = __any_sync(0xffffffffu, grow);
+        if (grow) {
+          corr = fast_exp2((m_ref - mt) * scale);
+          l *= corr;
+          m_ref = mt;
         }
       }
       // P = 2^((s - m_ref) * scale) <= 2^8, packed to 16 bits into S_i's first 64 columns.
@@ -480,6 +469,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       const float2 a = __fadd2_rn(a01, a23);
       l += a.x + a.y;
       tmem_st_64cols(t_row + col_s(i), pk);
+      if (rescale) {
+        // O_i holds P V over earlier tiles relative to the old m_ref (PV_{j-1} is
+        // complete: S_i of this tile was issued after it).
+        const float2 corr2 = make_float2(corr, corr);
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t o[32];
+          tmem_ld_32cols(t_row + col_o(i) + cc * 32, o);
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float2 v = __fmul2_rn(make_float2(__uint_as_float(o[c]), __uint_as_float(o[c + 1])), corr2);
+            o[c] = __float_as_uint(v.x);
+            o[c + 1] = __float_as_uint(v.y);
+          }
+          tmem_st_32cols(t_row + col_o(i) + cc * 32, o);
+        }
+      }
       tmem_wait_st();
       if (j == n_kv - 1 && kbase + kTileN - 1 > pos_max) {
         // Keys past the last visible one (pos_max) in the final KV tile are either
