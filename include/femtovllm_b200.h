@@ -88,6 +88,19 @@ FVB_API int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride
                       void* stream);
 
 /*
+ * slot_mapping[t] = block_tables[s][positions[t] / 16] * 16 + positions[t] % 16 for every
+ * token t of sequence s (cu_seqlens[s] <= t < cu_seqlens[s+1]); -1 where the table entry
+ * is -1 (the token is then skipped by fvb_store_kvcache).  cu_seqlens may be NULL for one
+ * token per sequence (decode).  The index arithmetic of the reference's KV-write loops
+ * (femtovllm/models/qwen/qwen3.py:250-264 decode, 335-361 prefill) on the device; the
+ * reference builds no slot mapping of its own (its metadata is assembled on the host in
+ * femtovllm/engine/model_runner.py:159-339).
+ */
+FVB_API int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const int32_t* cu_seqlens,
+                                   int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
+                                   int block_size, int64_t* slot_mapping, void* stream);
+
+/*
  * Decode paged attention (one query token per sequence), split-KV.
  *
  * Replaces PagedAttentionGemvCuda (csrc/paged_attention/paged_attention_gemv.cu:223-308,

@@ -185,6 +185,21 @@ int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_
                                           static_cast<cudaStream_t>(stream)));
 }
 
+int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const int32_t* cu_seqlens, int num_seqs,
+                           const int32_t* block_tables, int max_blocks_per_seq, int block_size,
+                           int64_t* slot_mapping, void* stream) {
+  if (num_tokens < 0 || num_seqs < 0 || max_blocks_per_seq < 0 || block_size <= 0) return FVB_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return FVB_OK;
+  if (!positions || !block_tables || !slot_mapping || num_seqs == 0) return FVB_ERR_INVALID_ARGUMENT;
+  if (!cu_seqlens && num_tokens > num_seqs) return FVB_ERR_INVALID_ARGUMENT;
+  cudaError_t e;
+  int* err = device_error_ptr(&e);
+  if (!err) return cuda_status(e);
+  return cuda_status(launch_build_slot_mapping(positions, num_tokens, cu_seqlens, num_seqs, block_tables,
+                                               max_blocks_per_seq, block_size, slot_mapping, err,
+                                               static_cast<cudaStream_t>(stream)));
+}
+
 size_t fvb_paged_attention_decode_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
                                                  int max_kv_len) {
   if (num_seqs <= 0 || !gqa_ok(n_heads, n_kv_heads)) return 0;

@@ -20,6 +20,10 @@ cudaError_t launch_store_kvcache(const void* k, const void* v, int64_t token_str
                                  int64_t num_tokens, int n_kv_heads, int head_dim, int block_size, int esize,
                                  int* err, cudaStream_t stream);
 
+cudaError_t launch_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const int32_t* cu_seqlens,
+                                      int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
+                                      int block_size, int64_t* slot_mapping, int* err, cudaStream_t stream);
+
 // Split-KV plan of one decode launch.  Deterministic in its inputs and the
 // device's SM count, so the workspace size can be asked for ahead of the call.
 struct DecodePlan {

@@ -110,4 +110,52 @@ cudaError_t launch_store_kvcache(const void* k, const void* v, int64_t token_str
   return cudaGetLastError();
 }
 
+// slot_mapping[t] = table[s][pos_t / P] * P + pos_t % P for every new token t
+// of sequence s, -1 when the table entry is -1 or pos_t lies outside the row.
+// The index arithmetic of the reference's write loops (qwen3.py:250-264
+// decode, 335-361 prefill), computed on the device.  cu_seqlens == nullptr
+// means one token per sequence (decode: token t belongs to sequence t).
+__global__ void __launch_bounds__(256) build_slot_mapping_kernel(const int32_t* __restrict__ positions,
+                                                                 int64_t num_tokens,
+                                                                 const int32_t* __restrict__ cu_seqlens, int num_seqs,
+                                                                 const int32_t* __restrict__ block_tables,
+                                                                 int max_blocks_per_seq, int block_size,
+                                                                 int64_t* __restrict__ slot_mapping, int* err) {
+  const int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (t >= num_tokens) return;
+  int s;
+  if (cu_seqlens == nullptr) {
+    s = int(t);
+  } else {
+    int lo = 0, hi = num_seqs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (__ldg(cu_seqlens + mid) <= t) lo = mid; else hi = mid - 1;
+    }
+    s = lo;
+  }
+  const int pos = __ldg(positions + t);
+  const int page = pos >= 0 ? pos / block_size : -1;
+  int64_t slot = -1;
+  if (page < 0 || page >= max_blocks_per_seq || s >= num_seqs) {
+    record_error(err, FVB_ERR_INVALID_ARGUMENT, int(t));
+  } else {
+    const int blk = __ldg(block_tables + int64_t(s) * max_blocks_per_seq + page);
+    if (blk >= 0) slot = int64_t(blk) * block_size + pos % block_size;
+  }
+  slot_mapping[t] = slot;
+}
+
+cudaError_t launch_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const int32_t* cu_seqlens,
+                                      int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
+                                      int block_size, int64_t* slot_mapping, int* err, cudaStream_t stream) {
+  if (num_tokens == 0) return cudaSuccess;
+  const int64_t blocks = (num_tokens + 255) / 256;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
+  build_slot_mapping_kernel<<<unsigned(blocks), 256, 0, stream>>>(positions, num_tokens, cu_seqlens, num_seqs,
+                                                                  block_tables, max_blocks_per_seq, block_size,
+                                                                  slot_mapping, err);
+  return cudaGetLastError();
+}
+
 }  // namespace fvb

@@ -148,6 +148,30 @@ void StoreKVCacheCuda(torch::Tensor k, torch::Tensor v, torch::Tensor k_pool, to
                "StoreKVCacheCuda");
 }
 
+torch::Tensor BuildSlotMappingCuda(torch::Tensor positions, std::optional<torch::Tensor> cu_seqlens,
+                                  torch::Tensor block_tables) {
+  TORCH_CHECK(positions.is_cuda() && block_tables.is_cuda(), "positions and block_tables must be CUDA tensors");
+  TORCH_CHECK(positions.scalar_type() == torch::kInt32 && block_tables.scalar_type() == torch::kInt32,
+              "positions and block_tables must be int32");
+  TORCH_CHECK(positions.is_contiguous() && block_tables.is_contiguous() && block_tables.dim() == 2,
+              "positions must be contiguous, block_tables (num_seqs, max_blocks) contiguous");
+  int num_seqs = int(block_tables.size(0));
+  const int32_t* cu = nullptr;
+  if (cu_seqlens.has_value()) {
+    TORCH_CHECK(cu_seqlens->is_cuda() && cu_seqlens->scalar_type() == torch::kInt32 && cu_seqlens->is_contiguous(),
+                "cu_seqlens must be a contiguous int32 CUDA tensor");
+    TORCH_CHECK(cu_seqlens->numel() == num_seqs + 1, "cu_seqlens must have num_seqs + 1 entries");
+    cu = cu_seqlens->data_ptr<int32_t>();
+  }
+  c10::cuda::CUDAGuard guard(positions.device());
+  auto slots = torch::empty({positions.numel()}, positions.options().dtype(torch::kInt64));
+  check_status(fvb_build_slot_mapping(positions.data_ptr<int32_t>(), positions.numel(), cu, num_seqs,
+                                      block_tables.data_ptr<int32_t>(), int(block_tables.size(1)), 16,
+                                      slots.data_ptr<int64_t>(), stream_of(positions)),
+               "BuildSlotMappingCuda");
+  return slots;
+}
+
 std::tuple<int64_t, int64_t> ReadDeviceError() {
   int code = 0, info = 0;
   check_status(fvb_read_device_error(&code, &info,
@@ -163,6 +187,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("PagedAttentionGemvCuda", &PagedAttentionGemvCuda, "decode paged attention (split-KV, sm_100a)");
   m.def("PagedAttentionGemmCuda", &PagedAttentionGemmCuda, "varlen chunked-prefill paged attention (sm_100a)");
   m.def("StoreKVCacheCuda", &StoreKVCacheCuda, "slot-mapped KV-cache write");
+  m.def("BuildSlotMappingCuda", &BuildSlotMappingCuda, "slot of every new token from positions and block tables",
+        py::arg("positions"), py::arg("cu_seqlens") = py::none(), py::arg("block_tables"));
   m.def("ReadDeviceError", &ReadDeviceError, "read and clear the device error word (synchronizes)");
 }
 
@@ -174,10 +200,12 @@ TORCH_LIBRARY(femtovllm_b200, m) {
       "paged_attention_prefill(Tensor q, Tensor k_pool, Tensor v_pool, Tensor cu_seqlens, int max_q_len, "
       "Tensor block_tables, Tensor kv_lens, Tensor positions) -> Tensor");
   m.def("store_kvcache(Tensor k, Tensor v, Tensor(a!) k_pool, Tensor(b!) v_pool, Tensor slot_mapping) -> ()");
+  m.def("build_slot_mapping(Tensor positions, Tensor? cu_seqlens, Tensor block_tables) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
   m.impl("paged_attention_decode", &PagedAttentionGemvCuda);
   m.impl("paged_attention_prefill", &PagedAttentionGemmCuda);
   m.impl("store_kvcache", &StoreKVCacheCuda);
+  m.impl("build_slot_mapping", &BuildSlotMappingCuda);
 }

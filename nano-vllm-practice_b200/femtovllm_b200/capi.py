@@ -45,6 +45,9 @@ _SIGNATURES = {
         [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,
          c_int, c_void_p],
     ),
+    "fvb_build_slot_mapping": (
+        c_int, [c_void_p, c_int64, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
+    ),
     "fvb_paged_attention_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "fvb_paged_attention_decode": (
         c_int,

@@ -10,7 +10,8 @@ Same function names, argument order and meaning, and error behaviour:
   ``ops/__init__.py:21-26``), read from the native module;
 
 plus ``store_kvcache``, the slot-mapped KV write that replaces the Python
-loops of ``femtovllm/models/qwen/qwen3.py:240-264, 322-366``.
+loops of ``femtovllm/models/qwen/qwen3.py:240-264, 322-366``, and
+``build_slot_mapping``, which computes its ``slot_mapping`` on the device.
 
 The reference routes each op through a Triton/CUDA backend switch
 (``femtovllm._DEV``, ``ImplCustomKernel``).  That router is gone: ``impl`` is
@@ -120,6 +121,23 @@ def store_kvcache(
     if slot_mapping.dtype != torch.int64:
         slot_mapping = slot_mapping.to(torch.int64)
     _cuda_backend.StoreKVCacheCuda(k, v, k_pool, v_pool, slot_mapping.contiguous())
+
+
+def build_slot_mapping(
+    positions: torch.Tensor,
+    block_tables: torch.Tensor,
+    cu_seqlens: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """int64 slot of every new token: ``table[s][pos // 16] * 16 + pos % 16`` (-1 for a -1 entry).
+
+    ``cu_seqlens`` (int32, ``num_seqs + 1``) maps tokens to sequences; ``None``
+    means one token per sequence (decode).  Computed on the device; it is the
+    index arithmetic of the reference write loops (``qwen3.py:250-264, 335-361``).
+    """
+    for t, n in ((positions, "positions"), (block_tables, "block_tables")):
+        if not t.is_cuda:
+            raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
+    return _cuda_backend.BuildSlotMappingCuda(positions.contiguous(), cu_seqlens, block_tables.contiguous())
 
 
 def read_device_error() -> tuple[int, int]:

@@ -279,3 +279,36 @@ def test_torch_ops_match_c_abi(cuda_device):
     assert (g.float() - a.float()).abs().max().item() <= 2e-2
     with pytest.raises(RuntimeError):
         ops.paged_attention_gemv(b.q.to(torch.float64), kp1, vp1, md["block_tables"], md["kv_lens"], b.max_kv_len)
+
+
+# ---------------------------------------------------------------------------
+# on-device slot mapping (the reference write loops' index arithmetic)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("make", [workloads.config3, workloads.config4, workloads.config1])
+def test_build_slot_mapping_matches_oracle(make, cuda_device):
+    from femtovllm_b200 import ops
+
+    b = make()
+    md = b.device_metadata(cuda_device)
+    slots = ops.build_slot_mapping(md["positions"], md["block_tables"], md["cu_seqlens"])
+    ref = oracle.build_slot_mapping(b.positions, b.seq_of_token, b.block_tables)
+    assert np.array_equal(slots.cpu().numpy(), ref)
+    if b.is_decode:  # one token per sequence: cu_seqlens may be omitted
+        assert torch.equal(ops.build_slot_mapping(md["positions"], md["block_tables"]), slots)
+
+
+def test_build_slot_mapping_edges(cuda_device):
+    from femtovllm_b200 import ops
+
+    tables = torch.tensor([[3, -1, 7], [5, 2, -1]], dtype=torch.int32, device=cuda_device)
+    pos = torch.tensor([0, 15, 16, 33, 0, 17, 40], dtype=torch.int32, device=cuda_device)
+    cu = torch.tensor([0, 4, 7], dtype=torch.int32, device=cuda_device)
+    cabi.read_device_error()
+    slots = ops.build_slot_mapping(pos, tables, cu).cpu().tolist()
+    # seq 0: 3*16+0, 3*16+15, page 1 is -1 -> -1, 7*16+1 ; seq 1: 5*16+0, 2*16+1, page 2 is -1 -> -1
+    assert slots == [48, 63, -1, 113, 80, 33, -1]
+    assert cabi.read_device_error() == (0, 0)
+    ops.build_slot_mapping(torch.tensor([48], dtype=torch.int32, device=cuda_device), tables[:1])  # page 3 > row
+    assert cabi.read_device_error()[0] == 1
