@@ -335,41 +335,60 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
 }
 
 // Merge the split partials of every (sequence, head) that has more than one
-// split.  One warp per (sequence, head); lane l owns dims [l*D/32, (l+1)*D/32).
+// split.  One CTA per (sequence, head), one thread per head dim: the split
+// weights 2^(lse_s - max) are computed once into shared memory, then every
+// thread sums its column of the partial rows (coalesced across threads).
 template <typename T, int D>
-__global__ void __launch_bounds__(256) decode_combine_kernel(const float* __restrict__ ws_o,
-                                                             const float* __restrict__ ws_lse, T* __restrict__ out,
-                                                             const int32_t* __restrict__ kv_lens, int kv_cap,
-                                                             int num_seqs, int n_heads, int pages_per_split,
-                                                             int max_splits) {
-  constexpr int kDPL = D / 32;
-  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (gw >= num_seqs * n_heads) return;
-  const int b = gw / n_heads, head = gw % n_heads;
+__global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restrict__ ws_o,
+                                                           const float* __restrict__ ws_lse, T* __restrict__ out,
+                                                           const int32_t* __restrict__ kv_lens, int kv_cap,
+                                                           int num_seqs, int n_heads, int pages_per_split,
+                                                           int max_splits) {
+  extern __shared__ float wsh[];  // [max_splits] weights, then [D / 32] partial maxima / sums
+  float* red = wsh + max_splits;
+  const int b = blockIdx.x / n_heads, head = blockIdx.x % n_heads;
+  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
   const int kv_len = min(max(__ldg(kv_lens + b), 0), kv_cap);
   const int npages = (kv_len + kPageSize - 1) / kPageSize;
   const int nsplits = (npages + pages_per_split - 1) / pages_per_split;
-  if (nsplits <= 1) return;
+  if (nsplits <= 1) return;  // written directly by the split kernel
   const int64_t base = (int64_t(b) * n_heads + head) * max_splits;
   float mx = -INFINITY;
-  for (int s = lane; s < nsplits; s += 32) mx = fmaxf(mx, ws_lse[base + s]);
+  for (int s = d; s < nsplits; s += D) {
+    const float v = __ldg(ws_lse + base + s);
+    wsh[s] = v;
+    mx = fmaxf(mx, v);
+  }
   mx = warp_max(mx);
-  float L = 0.f, o[kDPL];
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
 #pragma unroll
-  for (int i = 0; i < kDPL; ++i) o[i] = 0.f;
-  for (int s = 0; s < nsplits; ++s) {
-    const float w = fast_exp2(__ldg(ws_lse + base + s) - mx);
+  for (int w = 1; w < D / 32; ++w) mx = fmaxf(mx, red[w]);
+  __syncthreads();
+  float L = 0.f;
+  for (int s = d; s < nsplits; s += D) {
+    const float w = fast_exp2(wsh[s] - mx);
+    wsh[s] = w;
     L += w;
-    const float* src = ws_o + (base + s) * D + lane * kDPL;
-#pragma unroll
-    for (int i = 0; i < kDPL; ++i) o[i] = fmaf(w, __ldg(src + i), o[i]);
   }
-  const float inv = 1.f / L;
+  L = warp_sum(L);
+  if (lane == 0) red[warp] = L;
+  __syncthreads();
+  L = red[0];
 #pragma unroll
-  for (int i = 0; i < kDPL; ++i) {
-    out[(int64_t(head) * num_seqs + b) * D + lane * kDPL + i] = Elem<T>::from_f(o[i] * inv);
+  for (int w = 1; w < D / 32; ++w) L += red[w];
+  const float* src = ws_o + base * D + d;
+  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+  int s = 0;
+  for (; s + 4 <= nsplits; s += 4) {
+    o0 = fmaf(wsh[s], __ldg(src + int64_t(s) * D), o0);
+    o1 = fmaf(wsh[s + 1], __ldg(src + int64_t(s + 1) * D), o1);
+    o2 = fmaf(wsh[s + 2], __ldg(src + int64_t(s + 2) * D), o2);
+    o3 = fmaf(wsh[s + 3], __ldg(src + int64_t(s + 3) * D), o3);
   }
+  for (; s < nsplits; ++s) o0 = fmaf(wsh[s], __ldg(src + int64_t(s) * D), o0);
+  out[(int64_t(head) * num_seqs + b) * D + d] = Elem<T>::from_f(((o0 + o1) + (o2 + o3)) / L);
 }
 
 template <typename T, int D, int NREP>
@@ -404,10 +423,14 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
       ws_o, ws_lse, err);
   ce = cudaGetLastError();
   if (ce != cudaSuccess || plan.max_splits <= 1) return ce;
-  const int warps = num_seqs * n_kv_heads * NREP;
-  decode_combine_kernel<T, D><<<(warps + 7) / 8, 256, 0, stream>>>(ws_o, ws_lse, static_cast<T*>(out), kv_lens,
-                                                                   kv_cap, num_seqs, n_kv_heads * NREP,
-                                                                   plan.pages_per_split, plan.max_splits);
+  const size_t csmem = (size_t(plan.max_splits) + D / 32) * sizeof(float);
+  if (csmem > 48 * 1024) {
+    ce = cudaFuncSetAttribute(decode_combine_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(csmem));
+    if (ce != cudaSuccess) return ce;
+  }
+  decode_combine_kernel<T, D><<<unsigned(num_seqs * n_kv_heads * NREP), D, csmem, stream>>>(
+      ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap, num_seqs, n_kv_heads * NREP, plan.pages_per_split,
+      plan.max_splits);
   return cudaGetLastError();
 }
 
