@@ -318,9 +318,10 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seqs", type=int, default=24)
     ap.add_argument("--num-seqs", type=int, default=256, help="sequences per GPU (256 = BASELINE config 2)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long", "qk_norm_rope"],
                     help="decode = config 2 (the contract line); prefill = config 3; mixed = config 4; "
-                         "long = config 5 sharded over the ranks")
+                         "long = config 5 sharded over the ranks; qk_norm_rope = the fused q/k norm + rotary + "
+                         "KV write over config 3's new tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -409,7 +410,8 @@ def main():
 
 
 def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
-    """Development measurements: prefill (config 3), mixed (config 4), long decode (config 5)."""
+    """Development measurements: prefill (config 3), mixed (config 4), long decode (config 5), and the
+    fused q/k norm + rotary + KV write over config 3's new tokens."""
     import torch
     import torch.distributed as dist
 
@@ -417,7 +419,7 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    if args.workload == "prefill":
+    if args.workload in ("prefill", "qk_norm_rope"):
         batch = workloads.config3(seed=3 + rank)
     elif args.workload == "mixed":
         batch = workloads.config4(seed=4 + rank)
@@ -431,6 +433,28 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
         def step():
             return ops.paged_attention_gemv(batch.q, batch.k_pool, batch.v_pool, md["block_tables"], md["kv_lens"],
                                             batch.max_kv_len)
+    elif args.workload == "qk_norm_rope":
+        # The projection output (T, (Hq + 2 Hkv) D) as the Linear layers emit it; q / k / v are views of it.
+        T, Hq, Hkv, D = batch.num_tokens, batch.n_heads, batch.n_kv_heads, batch.head_dim
+        x = torch.cat([batch.q.transpose(0, 1).reshape(T, -1), batch.k_new.reshape(T, -1),
+                       batch.v_new.reshape(T, -1)], dim=1)
+        batch.q = None
+        qv = x[:, : Hq * D].view(T, Hq, D)
+        kv = x[:, Hq * D : (Hq + Hkv) * D].view(T, Hkv, D)
+        vv = x[:, (Hq + Hkv) * D :].view(T, Hkv, D)
+        g = torch.Generator(device=dev).manual_seed(7)
+        q_w = (1 + 0.25 * torch.randn(D, generator=g, device=dev)).to(batch.dtype)
+        k_w = (1 + 0.25 * torch.randn(D, generator=g, device=dev)).to(batch.dtype)
+        rows = int(batch.kv_lens.max())
+        inv = 1e-6 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D)
+        theta = torch.arange(rows, device=dev, dtype=torch.float32)[:, None] * inv[None]
+        theta = torch.cat([theta, theta], -1)
+        cos, sin = theta.cos().to(batch.dtype), theta.sin().to(batch.dtype)
+        es = x.element_size()
+
+        def step():
+            return ops.qk_norm_rope_store(qv, kv, vv, q_w, k_w, 1e-6, cos, sin, md["positions"], batch.k_pool,
+                                          batch.v_pool, md["slot_mapping"])
     else:
         def step():
             return ops.paged_attention_gemm(batch.q, batch.k_pool, batch.v_pool, md["cu_seqlens"], batch.max_q_len, 32,
@@ -448,8 +472,15 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
         ev1.record(stream)
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / args.steps
-    res = {"ms": ms, "flops": batch.attn_flops(), "bytes": batch.decode_bytes() if args.workload == "long"
-           else batch.kv_bytes(), "tokens": batch.num_tokens}
+    if args.workload == "long":
+        nbytes = batch.decode_bytes()
+    elif args.workload == "qk_norm_rope":
+        # q, k, v read once and q_out, k, v written once, plus position and slot per token
+        nbytes = 2 * batch.num_tokens * (batch.n_heads + 2 * batch.n_kv_heads) * batch.head_dim * es + 12 * batch.num_tokens
+    else:
+        nbytes = batch.kv_bytes()
+    res = {"ms": ms, "flops": 0 if args.workload == "qk_norm_rope" else batch.attn_flops(), "bytes": nbytes,
+           "tokens": batch.num_tokens}
     gathered = [None] * world
     if world > 1:
         dist.all_gather_object(gathered, res)

@@ -101,6 +101,32 @@ FVB_API int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens,
                                    int block_size, int64_t* slot_mapping, void* stream);
 
 /*
+ * Fused q/k RMSNorm + rotary embedding + KV-cache write, one pass over the projection outputs:
+ *   q_out[h][t][:]                      = rope(rmsnorm(q[t][h][:]) * q_norm_weight)
+ *   k_pool[slot / 16][h][slot % 16][:]  = rope(rmsnorm(k[t][h][:]) * k_norm_weight)
+ *   v_pool[slot / 16][h][slot % 16][:]  = v[t][h][:]   (bit-exact)
+ * rmsnorm(x) = x / sqrt(mean(x^2) + eps) over head_dim (nn.RMSNorm, femtovllm/models/qwen/qwen3.py:181-183);
+ * rope(y)[d] = y[d] * cos[p][d] + (d < D/2 ? -y[d + D/2] : y[d - D/2]) * sin[p][d] with p = positions[t]
+ * (QwenRotaryEmbedding.forward, qwen3.py:53-138; rope_cos / rope_sin are its [rope_rows][head_dim]
+ * buffers, in `dtype`).  Replaces qwen3.py:234-238 plus the KV-write loops (qwen3.py:240-264, 322-366)
+ * and the q transpose + contiguous copy before the attention op (qwen3.py:270, 372;
+ * femtovllm/ops/__init__.py:41-42): q_out is [n_heads][num_tokens][head_dim], the layout
+ * fvb_paged_attention_decode / _prefill take.  q / k / v are [num_tokens][heads][head_dim] with element
+ * strides (token_stride, head_stride, 1), e.g. views into one fused qkv projection output; every row
+ * start and every pointer must be 16-byte aligned.  slot_mapping as for fvb_store_kvcache (-1 skips the
+ * K/V write of a token; q_out is written regardless).  head_dim 64 or 128.  A position outside
+ * [0, rope_rows) records FVB_ERR_INVALID_ARGUMENT in the device error word and leaves that row unwritten.
+ */
+FVB_API int fvb_qk_norm_rope_store(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+                                   int64_t k_token_stride, int64_t k_head_stride, const void* v,
+                                   int64_t v_token_stride, int64_t v_head_stride, const void* q_norm_weight,
+                                   const void* k_norm_weight, float eps, const void* rope_cos, const void* rope_sin,
+                                   int rope_rows, const int32_t* positions, const int64_t* slot_mapping,
+                                   int64_t num_tokens, int n_heads, int n_kv_heads, int head_dim, void* q_out,
+                                   void* k_pool, void* v_pool, int64_t num_blocks, int block_size, int dtype,
+                                   void* stream);
+
+/*
  * Decode paged attention (one query token per sequence), split-KV.
  *
  * Replaces PagedAttentionGemvCuda (csrc/paged_attention/paged_attention_gemv.cu:223-308,

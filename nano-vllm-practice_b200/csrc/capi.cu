@@ -185,6 +185,46 @@ int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_
                                           static_cast<cudaStream_t>(stream)));
 }
 
+int fvb_qk_norm_rope_store(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+                           int64_t k_token_stride, int64_t k_head_stride, const void* v, int64_t v_token_stride,
+                           int64_t v_head_stride, const void* q_norm_weight, const void* k_norm_weight, float eps,
+                           const void* rope_cos, const void* rope_sin, int rope_rows, const int32_t* positions,
+                           const int64_t* slot_mapping, int64_t num_tokens, int n_heads, int n_kv_heads,
+                           int head_dim, void* q_out, void* k_pool, void* v_pool, int64_t num_blocks, int block_size,
+                           int dtype, void* stream) {
+  const int es = esize_of(dtype);
+  if (es == 0) return FVB_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return FVB_ERR_UNSUPPORTED;
+  if (num_tokens < 0 || n_heads <= 0 || n_kv_heads <= 0 || rope_rows <= 0 || block_size <= 0 || num_blocks < 0 ||
+      q_token_stride < 0 || q_head_stride < 0 || k_token_stride < 0 || k_head_stride < 0 || v_token_stride < 0 ||
+      v_head_stride < 0 || !(eps >= 0.f) || eps > 1.f)
+    return FVB_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return FVB_OK;
+  if (!q || !k || !v || !q_norm_weight || !k_norm_weight || !rope_cos || !rope_sin || !positions || !slot_mapping ||
+      !q_out || !k_pool || !v_pool)
+    return FVB_ERR_INVALID_ARGUMENT;
+  // One 16-byte vector per lane: every row start must be 16-byte aligned.
+  const void* vec_ptrs[] = {q, k, v, q_norm_weight, k_norm_weight, rope_cos, rope_sin, q_out, k_pool, v_pool};
+  for (const void* p : vec_ptrs) {
+    if (!aligned16(p)) return FVB_ERR_MISALIGNED;
+  }
+  const int64_t strides[] = {q_token_stride, q_head_stride, k_token_stride, k_head_stride, v_token_stride,
+                             v_head_stride};
+  for (int64_t st : strides) {
+    if ((st * es) % 16 != 0) return FVB_ERR_MISALIGNED;
+  }
+  if ((reinterpret_cast<uintptr_t>(slot_mapping) & 7) != 0 || (reinterpret_cast<uintptr_t>(positions) & 3) != 0)
+    return FVB_ERR_MISALIGNED;
+  cudaError_t e;
+  int* err = device_error_ptr(&e);
+  if (!err) return cuda_status(e);
+  return cuda_status(launch_qk_norm_rope_store(
+      q, q_token_stride, q_head_stride, k, k_token_stride, k_head_stride, v, v_token_stride, v_head_stride,
+      q_norm_weight, k_norm_weight, eps, rope_cos, rope_sin, rope_rows, positions, slot_mapping, num_tokens, n_heads,
+      n_kv_heads, head_dim, q_out, k_pool, v_pool, num_blocks, block_size, dtype, err,
+      static_cast<cudaStream_t>(stream)));
+}
+
 int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const int32_t* cu_seqlens, int num_seqs,
                            const int32_t* block_tables, int max_blocks_per_seq, int block_size,
                            int64_t* slot_mapping, void* stream) {

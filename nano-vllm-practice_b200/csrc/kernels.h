@@ -58,6 +58,16 @@ cudaError_t launch_prefill_simt(const void* q, void* out, const void* k_pool, co
                                 const int32_t* kv_lens, const int32_t* positions, int dtype, int* err,
                                 cudaStream_t stream);
 
+// Fused q/k RMSNorm + rotary embedding + K/V pool write (qk_norm_rope.cu).
+// Strides are in elements; q_out is [n_heads][num_tokens][head_dim].
+cudaError_t launch_qk_norm_rope_store(const void* q, int64_t q_ts, int64_t q_hs, const void* k, int64_t k_ts,
+                                      int64_t k_hs, const void* v, int64_t v_ts, int64_t v_hs, const void* q_w,
+                                      const void* k_w, float eps, const void* cos_t, const void* sin_t, int rope_rows,
+                                      const int32_t* positions, const int64_t* slot_mapping, int64_t num_tokens,
+                                      int n_heads, int n_kv_heads, int head_dim, void* q_out, void* k_pool,
+                                      void* v_pool, int64_t num_blocks, int block_size, int dtype, int* err,
+                                      cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace fvb

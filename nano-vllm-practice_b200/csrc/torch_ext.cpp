@@ -4,7 +4,8 @@
 // the same entry-point names and argument order (PagedAttentionGemvCuda,
 // PagedAttentionGemmCuda) and the same attributes (kMaxKVLenNonSplit,
 // kKVLenPerPage, kDimHead), plus StoreKVCacheCuda for the slot-mapped KV write
-// the reference does in Python.  Each function validates like the reference's
+// the reference does in Python and QKNormRopeStoreCuda for the fused q/k
+// norm + rotary embedding + KV write.  Each function validates like the reference's
 // TORCH_CHECKs (csrc/paged_attention/paged_attention_gemv.cu:231-274,
 // paged_attention_gemm.cu:314-358), allocates the output (and the split-KV
 // workspace) with the caching allocator, and calls the C ABI on the current
@@ -148,6 +149,49 @@ void StoreKVCacheCuda(torch::Tensor k, torch::Tensor v, torch::Tensor k_pool, to
                "StoreKVCacheCuda");
 }
 
+// Fused q/k RMSNorm + rotary embedding + KV write; returns q in the head-major
+// (n_heads, num_tokens, d_head) layout the attention ops take.
+torch::Tensor QKNormRopeStoreCuda(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor q_norm_weight,
+                                  torch::Tensor k_norm_weight, double eps, torch::Tensor rope_cos,
+                                  torch::Tensor rope_sin, torch::Tensor positions, torch::Tensor k_pool,
+                                  torch::Tensor v_pool, torch::Tensor slot_mapping) {
+  const std::vector<at::Tensor> all = {q, k, v, q_norm_weight, k_norm_weight, rope_cos, rope_sin, positions,
+                                       k_pool, v_pool, slot_mapping};
+  for (const auto& t : all) TORCH_CHECK(t.is_cuda() && t.get_device() == q.get_device(), "all arguments must be CUDA tensors on one device");
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "q, k, v must be (num_tokens, heads, d_head)");
+  TORCH_CHECK(q.stride(2) == 1 && k.stride(2) == 1 && v.stride(2) == 1, "d_head must be the contiguous dimension of q, k, v");
+  TORCH_CHECK(k.sizes() == v.sizes() && q.size(0) == k.size(0) && q.size(2) == k.size(2), "q / k / v shapes differ");
+  const int64_t D = q.size(2);
+  TORCH_CHECK(q_norm_weight.dim() == 1 && k_norm_weight.dim() == 1 && q_norm_weight.numel() == D &&
+                  k_norm_weight.numel() == D && q_norm_weight.is_contiguous() && k_norm_weight.is_contiguous(),
+              "norm weights must be contiguous (d_head,) tensors");
+  TORCH_CHECK(rope_cos.dim() == 2 && rope_cos.sizes() == rope_sin.sizes() && rope_cos.size(1) == D &&
+                  rope_cos.is_contiguous() && rope_sin.is_contiguous(),
+              "rope_cos / rope_sin must be contiguous (rows, d_head) tensors");
+  TORCH_CHECK(positions.scalar_type() == torch::kInt32 && positions.is_contiguous() && positions.numel() == q.size(0),
+              "positions must be a contiguous int32 tensor with one entry per token");
+  TORCH_CHECK(slot_mapping.scalar_type() == torch::kInt64 && slot_mapping.is_contiguous() &&
+                  slot_mapping.numel() == q.size(0),
+              "slot_mapping must be a contiguous int64 tensor with one entry per token");
+  TORCH_CHECK(k_pool.dim() == 4 && k_pool.sizes() == v_pool.sizes() && k_pool.is_contiguous() && v_pool.is_contiguous(),
+              "pools must be contiguous (num_blocks, n_kv_heads, block_size, d_head)");
+  TORCH_CHECK(k_pool.size(1) == k.size(1) && k_pool.size(3) == D, "pool and k head shapes differ");
+  const auto dt = q.scalar_type();
+  for (const auto& t : {k, v, q_norm_weight, k_norm_weight, rope_cos, rope_sin, k_pool, v_pool})
+    TORCH_CHECK(t.scalar_type() == dt, "q, k, v, the norm weights, the rope tables and the pools must share a dtype");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto q_out = torch::empty({q.size(1), q.size(0), D}, q.options());
+  check_status(fvb_qk_norm_rope_store(q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1),
+                                      v.data_ptr(), v.stride(0), v.stride(1), q_norm_weight.data_ptr(),
+                                      k_norm_weight.data_ptr(), float(eps), rope_cos.data_ptr(), rope_sin.data_ptr(),
+                                      int(rope_cos.size(0)), positions.data_ptr<int32_t>(),
+                                      slot_mapping.data_ptr<int64_t>(), q.size(0), int(q.size(1)), int(k.size(1)),
+                                      int(D), q_out.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_pool.size(0),
+                                      int(k_pool.size(2)), dtype_code(dt), stream_of(q)),
+               "QKNormRopeStoreCuda");
+  return q_out;
+}
+
 torch::Tensor BuildSlotMappingCuda(torch::Tensor positions, std::optional<torch::Tensor> cu_seqlens,
                                   torch::Tensor block_tables) {
   TORCH_CHECK(positions.is_cuda() && block_tables.is_cuda(), "positions and block_tables must be CUDA tensors");
@@ -189,6 +233,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("StoreKVCacheCuda", &StoreKVCacheCuda, "slot-mapped KV-cache write");
   m.def("BuildSlotMappingCuda", &BuildSlotMappingCuda, "slot of every new token from positions and block tables",
         py::arg("positions"), py::arg("cu_seqlens") = py::none(), py::arg("block_tables"));
+  m.def("QKNormRopeStoreCuda", &QKNormRopeStoreCuda,
+        "fused q/k RMSNorm + rotary embedding + KV-cache write; returns q as (n_heads, num_tokens, d_head)");
   m.def("ReadDeviceError", &ReadDeviceError, "read and clear the device error word (synchronizes)");
 }
 
@@ -201,6 +247,10 @@ TORCH_LIBRARY(femtovllm_b200, m) {
       "Tensor block_tables, Tensor kv_lens, Tensor positions) -> Tensor");
   m.def("store_kvcache(Tensor k, Tensor v, Tensor(a!) k_pool, Tensor(b!) v_pool, Tensor slot_mapping) -> ()");
   m.def("build_slot_mapping(Tensor positions, Tensor? cu_seqlens, Tensor block_tables) -> Tensor");
+  m.def(
+      "qk_norm_rope_store(Tensor q, Tensor k, Tensor v, Tensor q_norm_weight, Tensor k_norm_weight, float eps, "
+      "Tensor rope_cos, Tensor rope_sin, Tensor positions, Tensor(a!) k_pool, Tensor(b!) v_pool, "
+      "Tensor slot_mapping) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
@@ -208,4 +258,5 @@ TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
   m.impl("paged_attention_prefill", &PagedAttentionGemmCuda);
   m.impl("store_kvcache", &StoreKVCacheCuda);
   m.impl("build_slot_mapping", &BuildSlotMappingCuda);
+  m.impl("qk_norm_rope_store", &QKNormRopeStoreCuda);
 }

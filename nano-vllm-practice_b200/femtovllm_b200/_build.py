@@ -48,7 +48,15 @@ NVCC_FLAGS = ARCH + [
     f"-I{INCLUDE}",
     f"-I{CSRC}",
 ]
-CU_SOURCES = ["capi.cu", "store_kvcache.cu", "decode.cu", "decode_noalloc.cu", "prefill_simt.cu", "prefill_sm100.cu"]
+CU_SOURCES = [
+    "capi.cu",
+    "store_kvcache.cu",
+    "qk_norm_rope.cu",
+    "decode.cu",
+    "decode_noalloc.cu",
+    "prefill_simt.cu",
+    "prefill_sm100.cu",
+]
 
 
 def _headers() -> list[Path]:

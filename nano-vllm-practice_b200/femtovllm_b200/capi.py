@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import ctypes
 import re
-from ctypes import c_int, c_int64, c_size_t, c_void_p, c_char_p
+from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
 from femtovllm_b200 import LIB_PATH
@@ -47,6 +47,12 @@ _SIGNATURES = {
     ),
     "fvb_build_slot_mapping": (
         c_int, [c_void_p, c_int64, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
+    ),
+    "fvb_qk_norm_rope_store": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+         c_float, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p,
+         c_void_p, c_int64, c_int, c_int, c_void_p],
     ),
     "fvb_paged_attention_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "fvb_paged_attention_decode": (

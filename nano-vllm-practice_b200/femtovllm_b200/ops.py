@@ -10,8 +10,10 @@ Same function names, argument order and meaning, and error behaviour:
   ``ops/__init__.py:21-26``), read from the native module;
 
 plus ``store_kvcache``, the slot-mapped KV write that replaces the Python
-loops of ``femtovllm/models/qwen/qwen3.py:240-264, 322-366``, and
-``build_slot_mapping``, which computes its ``slot_mapping`` on the device.
+loops of ``femtovllm/models/qwen/qwen3.py:240-264, 322-366``,
+``build_slot_mapping``, which computes its ``slot_mapping`` on the device, and
+``qk_norm_rope_store``, which fuses the q/k RMSNorm and rotary embedding of
+``qwen3.py:234-238`` with that write and hands q back head-major.
 
 The reference routes each op through a Triton/CUDA backend switch
 (``femtovllm._DEV``, ``ImplCustomKernel``).  That router is gone: ``impl`` is
@@ -138,6 +140,46 @@ def build_slot_mapping(
         if not t.is_cuda:
             raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
     return _cuda_backend.BuildSlotMappingCuda(positions.contiguous(), cu_seqlens, block_tables.contiguous())
+
+
+def qk_norm_rope_store(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    q_norm_weight: torch.Tensor,
+    k_norm_weight: torch.Tensor,
+    eps: float,
+    rope_cos: torch.Tensor,
+    rope_sin: torch.Tensor,
+    positions: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    slot_mapping: torch.Tensor,
+) -> torch.Tensor:
+    """q/k RMSNorm + rotary embedding + KV write in one pass; returns q as ``(n_heads, T, d_head)``.
+
+    Does what ``QwenSelfAttention`` does between its projections and the
+    attention op (``qwen3.py:234-238`` then the write loops ``:240-264`` /
+    ``:322-366`` and ``q.transpose(0, 1)``): ``q``/``k`` are normalised over
+    ``d_head`` (``x / sqrt(mean(x^2) + eps) * weight``), rotated with the
+    rotary module's ``cos``/``sin`` buffers (``(rows, d_head)``) at
+    ``positions[t]``, k and v land in ``slot_mapping[t]`` (``-1`` skips) and
+    the returned q is ready for ``paged_attention_gemv`` / ``_gemm``.
+    ``q``, ``k``, ``v`` are ``(T, heads, d_head)`` views (e.g. of the
+    projection outputs) with ``d_head`` contiguous and 16-byte aligned rows.
+    """
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (k_pool, "k_pool"), (v_pool, "v_pool"), (positions, "positions"),
+                 (slot_mapping, "slot_mapping"), (rope_cos, "rope_cos"), (rope_sin, "rope_sin")):
+        if not t.is_cuda:
+            raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
+    if slot_mapping.dtype != torch.int64:
+        slot_mapping = slot_mapping.to(torch.int64)
+    if positions.dtype != torch.int32:
+        positions = positions.to(torch.int32)
+    return _cuda_backend.QKNormRopeStoreCuda(
+        q, k, v, q_norm_weight.contiguous(), k_norm_weight.contiguous(), float(eps), rope_cos.contiguous(),
+        rope_sin.contiguous(), positions.contiguous(), k_pool, v_pool, slot_mapping.contiguous()
+    )
 
 
 def read_device_error() -> tuple[int, int]:

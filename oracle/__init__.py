@@ -7,7 +7,9 @@ parts of the attention hot path:
 * the KV-cache write (the reference's per-sequence block-walk loops, and the
   equivalent ``slot_mapping`` scatter),
 * decode paged attention over ``block_tables`` with GQA,
-* varlen chunked-prefill causal attention over prefix-cached paged KV.
+* varlen chunked-prefill causal attention over prefix-cached paged KV,
+* the stage before them: q/k RMSNorm, rotary embedding and the KV write
+  (``oracle/qk_norm_rope.py``).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 ``--impl reference`` legs of ``bench.py`` may import it, and only as the
@@ -17,8 +19,10 @@ checker or the timed CPU baseline.  The product path
 Parity pin: ``tests/golden/*.npz`` were produced by running the reference's
 own ``QwenSelfAttention.forward_varlen_pytorch`` and its KV-write loops
 (``femtovllm/models/qwen/qwen3.py:240-264, 322-366, 389-544``) on CPU, by
-``tests/golden/make_golden.py``.  ``tests/test_oracle_golden.py`` checks this
-package against every one of those fixtures.
+``tests/golden/make_golden.py``; the ``norm_rope_*`` fixtures record the
+reference's q_norm / k_norm / QwenRotaryEmbedding and write loop
+(``qwen3.py:17-138, 181-183, 228-264, 308-366``).  ``tests/test_oracle_golden.py``
+checks this package against every one of those fixtures.
 """
 
 from oracle.paged_attention import (  # noqa: F401
@@ -29,4 +33,10 @@ from oracle.paged_attention import (  # noqa: F401
     store_kvcache,
     store_kvcache_decode_loop,
     store_kvcache_prefill_loop,
+)
+from oracle.qk_norm_rope import (  # noqa: F401
+    apply_rope,
+    qk_norm_rope_store,
+    rms_norm,
+    rope_tables,
 )

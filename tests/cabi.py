@@ -67,3 +67,21 @@ def read_device_error():
     code, info = ctypes.c_int(0), ctypes.c_int(0)
     capi.check(lib().fvb_read_device_error(ctypes.byref(code), ctypes.byref(info), _stream()), "read_device_error")
     return code.value, info.value
+
+
+def qk_norm_rope_store_status(q, k, v, q_w, k_w, eps, cos, sin, positions, k_pool, v_pool, slot_mapping, q_out):
+    """Raw status of fvb_qk_norm_rope_store (q / k / v: (T, heads, D) strided views)."""
+    return lib().fvb_qk_norm_rope_store(
+        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(), v.stride(0),
+        v.stride(1), q_w.data_ptr(), k_w.data_ptr(), float(eps), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+        positions.data_ptr(), slot_mapping.data_ptr(), q.shape[0], q.shape[1], k.shape[1], q.shape[2],
+        q_out.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_pool.shape[0], k_pool.shape[2],
+        capi.dtype_code(q.dtype), _stream(),
+    )
+
+
+def qk_norm_rope_store(q, k, v, q_w, k_w, eps, cos, sin, positions, k_pool, v_pool, slot_mapping):
+    q_out = torch.empty((q.shape[1], q.shape[0], q.shape[2]), dtype=q.dtype, device=q.device)
+    st = qk_norm_rope_store_status(q, k, v, q_w, k_w, eps, cos, sin, positions, k_pool, v_pool, slot_mapping, q_out)
+    capi.check(st, "fvb_qk_norm_rope_store")
+    return q_out

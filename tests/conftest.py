@@ -46,7 +46,24 @@ def golden_after(d: dict, which: str) -> np.ndarray:
     return pool
 
 
-GOLDEN_CASES = sorted(p.stem for p in GOLDEN.glob("*.npz"))
+GOLDEN_CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("norm_rope_"))
+NORM_ROPE_CASES = sorted(p.stem for p in GOLDEN.glob("norm_rope_*.npz"))
+
+
+def load_norm_rope(name: str) -> dict:
+    """Decode one norm_rope_* fixture (q/k RMSNorm + rotary embedding + KV write stage)."""
+    z = np.load(GOLDEN / f"{name}.npz")
+    d = {k: z[k] for k in z.files}
+    for k in ("q", "k_new", "v_new", "k_pool", "v_pool", "q_norm_weight", "k_norm_weight"):
+        d[k] = _bits_to_f32(d.pop(f"{k}_bits"))
+    d["v_written_rows"] = _bits_to_f32(d.pop("v_written_bits"))
+    d["k_written_rows"] = d.pop("k_written")
+    for k in ("n_heads", "n_kv_heads", "head_dim", "num_blocks", "rope_rows"):
+        d[k] = int(d[k])
+    d["eps"] = float(d["eps"])
+    q_lens = d["q_lens"]
+    d["seq_of_token"] = np.repeat(np.arange(len(q_lens)), q_lens)
+    return d
 
 
 @pytest.fixture(scope="session")

@@ -20,7 +20,14 @@ and o_proj are identities, and runs:
   ``qwen3.py:322-366``), with the attention op replaced by a stub -> the pools
   after that loop.
 
-All values are bf16-representable (stored as bf16 bits) so one fixture serves
+The ``norm_rope_*`` fixtures instead keep the reference's q_norm / k_norm
+(``nn.RMSNorm``, ``qwen3.py:181-183``, with seeded weights) and its
+``QwenRotaryEmbedding`` (``qwen3.py:17-138``), and record the q that
+``forward_varlen_custom_gemm`` / ``_gemv`` hand to the attention op plus the
+pool rows their write loops produce: the stage that ``qk_norm_rope_store``
+fuses.
+
+All inputs are bf16-representable (stored as bf16 bits) so one fixture serves
 both the fp32 and the bf16 checks; the reference runs in fp32.  Each fixture
 stores the pools before the write and only the rows the reference changed.
 """
@@ -147,34 +154,16 @@ def cases():
     return out
 
 
-def run_reference(case, femtovllm, QwenSelfAttention, VarlenAttnMetadata):
-    Hq, Hkv, D = case["Hq"], case["Hkv"], case["D"]
-    kv_lens, q_lens = case["kv_lens"], case["q_lens"]
-    B = len(kv_lens)
-    T = int(q_lens.sum())
+def _varlen_metadata(kv_lens, q_lens, tables, VarlenAttnMetadata):
+    """The reference's VarlenAttnMetadata (femtovllm/protocol.py:58-81) for one batch."""
     raw_cu = [0] + np.cumsum(q_lens).tolist()
     raw_pos = []
     for kl, ql in zip(kv_lens, q_lens):
         raw_pos.extend(range(int(kl) - int(ql), int(kl)))
-    raw_tables = [list(map(int, t)) for t in case["tables"]]
+    raw_tables = [list(map(int, t)) for t in tables]
     width = max(len(t) for t in raw_tables)
     padded = [t + [-1] * (width - len(t)) for t in raw_tables]
     is_decoding = bool((q_lens == 1).all())
-
-    cfg = types.SimpleNamespace(head_dim=D, rms_norm_eps=1e-6)
-    d_model = D * (Hq + 2 * Hkv)
-    attn = QwenSelfAttention(d_model, Hq, Hkv, max_seqlen=4, dropout_p=0.0, config=cfg)
-    attn.w_q = _Slice(0, Hq * D)
-    attn.w_k = _Slice(Hq * D, (Hq + Hkv) * D)
-    attn.w_v = _Slice((Hq + Hkv) * D, (Hq + 2 * Hkv) * D)
-    attn.q_norm = torch.nn.Identity()
-    attn.k_norm = torch.nn.Identity()
-    attn.rotary_embd = _NoRope()
-    attn.o_proj = torch.nn.Identity()
-    attn.eval()
-
-    q_tok = case["q"].transpose(0, 1).reshape(T, Hq * D)
-    x = torch.cat([q_tok, case["k_new"].reshape(T, Hkv * D), case["v_new"].reshape(T, Hkv * D)], dim=1)
     Q_TILE = 32
     cu_tiles, tile_seq = [0], []
     for s, ql in enumerate(q_lens):
@@ -200,6 +189,29 @@ def run_reference(case, femtovllm, QwenSelfAttention, VarlenAttnMetadata):
         raw_block_tables=raw_tables,
         is_decoding=is_decoding,
     )
+    return md, padded, raw_cu, raw_pos, is_decoding
+
+
+def run_reference(case, femtovllm, QwenSelfAttention, VarlenAttnMetadata):
+    Hq, Hkv, D = case["Hq"], case["Hkv"], case["D"]
+    kv_lens, q_lens = case["kv_lens"], case["q_lens"]
+    T = int(q_lens.sum())
+    md, padded, raw_cu, raw_pos, is_decoding = _varlen_metadata(kv_lens, q_lens, case["tables"], VarlenAttnMetadata)
+
+    cfg = types.SimpleNamespace(head_dim=D, rms_norm_eps=1e-6)
+    d_model = D * (Hq + 2 * Hkv)
+    attn = QwenSelfAttention(d_model, Hq, Hkv, max_seqlen=4, dropout_p=0.0, config=cfg)
+    attn.w_q = _Slice(0, Hq * D)
+    attn.w_k = _Slice(Hq * D, (Hq + Hkv) * D)
+    attn.w_v = _Slice((Hq + Hkv) * D, (Hq + 2 * Hkv) * D)
+    attn.q_norm = torch.nn.Identity()
+    attn.k_norm = torch.nn.Identity()
+    attn.rotary_embd = _NoRope()
+    attn.o_proj = torch.nn.Identity()
+    attn.eval()
+
+    q_tok = case["q"].transpose(0, 1).reshape(T, Hq * D)
+    x = torch.cat([q_tok, case["k_new"].reshape(T, Hkv * D), case["v_new"].reshape(T, Hkv * D)], dim=1)
     kp, vp = case["k_pool"].clone(), case["v_pool"].clone()
     with torch.no_grad():
         o, _ = attn.forward_varlen_pytorch(x, kp, vp, md)
@@ -222,6 +234,92 @@ def run_reference(case, femtovllm, QwenSelfAttention, VarlenAttnMetadata):
     return out, (kp, vp), (kp2, vp2), padded, raw_cu, raw_pos
 
 
+def norm_rope_cases():
+    """Cases for the q/k RMSNorm + rotary embedding + KV write stage (qwen3.py:228-264, 322-366)."""
+    out = []
+    # Attention is stubbed here, so only the pages that receive new tokens need
+    # real blocks: the cached-prefix pages of every table row point at block 0.
+    def tables_for(kv, q, num_blocks, seed):
+        rng = np.random.default_rng(seed)
+        free = [int(b) for b in rng.permutation(np.arange(1, num_blocks))]
+        rows = []
+        for kl, ql in zip(kv, q):
+            first, last = (int(kl) - int(ql)) // PAGE, (int(kl) - 1) // PAGE
+            rows.append([0] * first + [free.pop() for _ in range(first, last + 1)])
+        return rows
+
+    # Prefill chunks over cached prefixes, GQA 4, D 128, positions up to ~3000.
+    c = np.array([5, 17, 40])
+    p = np.array([0, 983, 2960])
+    case = _make_case("norm_rope_prefill", p + c, c, 8, 2, 128, 12, tables_for(p + c, c, 12, 21), 31)
+    case["rope_rows"] = 4096
+    out.append(case)
+    # Decode, MHA, D 64, kv_lens on and next to page boundaries.
+    kv = np.array([1, 16, 17, 640, 1999, 2048])
+    case = _make_case("norm_rope_decode_d64", kv, [1] * 6, 4, 4, 64, 10, tables_for(kv, [1] * 6, 10, 22), 32)
+    case["rope_rows"] = 2048
+    out.append(case)
+    return out
+
+
+def run_reference_norm_rope(case, femtovllm, QwenSelfAttention, VarlenAttnMetadata):
+    """The reference's own q_norm / k_norm (nn.RMSNorm), QwenRotaryEmbedding (base 1e6) and KV-write
+    loop, with the attention op replaced by a stub that records the q it is given."""
+    Hq, Hkv, D = case["Hq"], case["Hkv"], case["D"]
+    kv_lens, q_lens = case["kv_lens"], case["q_lens"]
+    T = int(q_lens.sum())
+    md, padded, raw_cu, raw_pos, is_decoding = _varlen_metadata(kv_lens, q_lens, case["tables"], VarlenAttnMetadata)
+    eps = 1e-6
+    cfg = types.SimpleNamespace(head_dim=D, rms_norm_eps=eps)
+    d_model = D * (Hq + 2 * Hkv)
+    attn = QwenSelfAttention(d_model, Hq, Hkv, max_seqlen=case["rope_rows"], dropout_p=0.0, config=cfg)
+    attn.w_q = _Slice(0, Hq * D)
+    attn.w_k = _Slice(Hq * D, (Hq + Hkv) * D)
+    attn.w_v = _Slice((Hq + Hkv) * D, (Hq + 2 * Hkv) * D)
+    gen = torch.Generator().manual_seed(int(case["kv_lens"].sum()))
+    q_w = (1.0 + 0.25 * torch.randn(D, generator=gen)).to(torch.bfloat16).to(torch.float32)
+    k_w = (1.0 + 0.25 * torch.randn(D, generator=gen)).to(torch.bfloat16).to(torch.float32)
+    with torch.no_grad():
+        attn.q_norm.weight.copy_(q_w)
+        attn.k_norm.weight.copy_(k_w)
+    attn.o_proj = torch.nn.Identity()
+    attn.eval()
+    q_tok = case["q"].transpose(0, 1).reshape(T, Hq * D)
+    x = torch.cat([q_tok, case["k_new"].reshape(T, Hkv * D), case["v_new"].reshape(T, Hkv * D)], dim=1)
+    seen = {}
+
+    def stub(q, **kw):
+        seen["q"] = q.detach().clone()
+        return torch.zeros_like(q)
+
+    kp, vp = case["k_pool"].clone(), case["v_pool"].clone()
+    saved = (femtovllm.ops.paged_attention_gemv, femtovllm.ops.paged_attention_gemm)
+    femtovllm.ops.paged_attention_gemv = stub
+    femtovllm.ops.paged_attention_gemm = stub
+    try:
+        with torch.no_grad():
+            if is_decoding:
+                attn.forward_varlen_custom_gemv(x, kp, vp, md)
+            else:
+                attn.forward_varlen_custom_gemm(x, kp, vp, md)
+    finally:
+        femtovllm.ops.paged_attention_gemv, femtovllm.ops.paged_attention_gemm = saved
+    pos = torch.tensor(raw_pos, dtype=torch.long)
+    return {
+        "q_ref": seen["q"].numpy().astype(np.float32),  # (Hq, T, D), as handed to the attention op
+        "k_pool": kp,
+        "v_pool": vp,
+        "q_norm_weight": q_w,
+        "k_norm_weight": k_w,
+        "eps": eps,
+        "cos_rows": attn.rotary_embd.cos[pos].numpy().astype(np.float32),
+        "sin_rows": attn.rotary_embd.sin[pos].numpy().astype(np.float32),
+        "padded": padded,
+        "cu": raw_cu,
+        "pos": raw_pos,
+    }
+
+
 def _bits(t: torch.Tensor) -> np.ndarray:
     return t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
 
@@ -235,8 +333,46 @@ def _changed_rows(before, after):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--which", choices=["attention", "norm_rope", "all"], default="all")
     args = ap.parse_args()
     femtovllm, QSA, VAM = _import_reference(args.reference)
+    if args.which in ("norm_rope", "all"):
+        for case in norm_rope_cases():
+            r = run_reference_norm_rope(case, femtovllm, QSA, VAM)
+            k_idx, _ = _changed_rows(case["k_pool"], r["k_pool"])
+            v_idx, v_rows = _changed_rows(case["v_pool"], r["v_pool"])
+            k_rows = r["k_pool"][k_idx[:, 0], k_idx[:, 1], k_idx[:, 2]].numpy().astype(np.float32)
+            np.savez_compressed(
+                HERE / f"{case['name']}.npz",
+                n_heads=case["Hq"],
+                n_kv_heads=case["Hkv"],
+                head_dim=case["D"],
+                num_blocks=case["num_blocks"],
+                rope_rows=case["rope_rows"],
+                eps=np.float32(r["eps"]),
+                kv_lens=case["kv_lens"],
+                q_lens=case["q_lens"],
+                cu_seqlens=np.asarray(r["cu"], np.int32),
+                positions=np.asarray(r["pos"], np.int32),
+                block_tables=np.asarray(r["padded"], np.int32),
+                q_bits=_bits(case["q"].transpose(0, 1).contiguous()),  # (T, Hq, D): the projection output
+                k_new_bits=_bits(case["k_new"]),
+                v_new_bits=_bits(case["v_new"]),
+                q_norm_weight_bits=_bits(r["q_norm_weight"]),
+                k_norm_weight_bits=_bits(r["k_norm_weight"]),
+                cos_rows=r["cos_rows"],
+                sin_rows=r["sin_rows"],
+                k_pool_bits=_bits(case["k_pool"]),
+                v_pool_bits=_bits(case["v_pool"]),
+                k_written_idx=k_idx,
+                k_written=k_rows,
+                v_written_idx=v_idx,
+                v_written_bits=v_rows,
+                q_ref=r["q_ref"],
+            )
+            print(f"{case['name']}: T={int(case['q_lens'].sum())} rows written={len(k_idx)}")
+    if args.which == "norm_rope":
+        return
     for case in cases():
         out, (kp, vp), (kp2, vp2), padded, cu, pos = run_reference(case, femtovllm, QSA, VAM)
         k_rows_idx, k_rows = _changed_rows(case["k_pool"], kp)

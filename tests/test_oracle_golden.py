@@ -68,3 +68,55 @@ def test_oracle_catches_a_planted_mask_error():
     n_rep = hq // kp.shape[1]
     bad = oracle.paged_attention._attend(d["q"][:n_rep, q0:q1], ks[0], vs[0], bad_visible, np.float64)
     assert np.abs(bad - d["out_ref"][:n_rep, q0:q1]).max() > 1e-3
+
+
+# ---------------------------------------------------------------------------
+# q/k RMSNorm + rotary embedding + KV write (norm_rope_* fixtures)
+# ---------------------------------------------------------------------------
+
+from conftest import NORM_ROPE_CASES, load_norm_rope  # noqa: E402
+
+
+@pytest.mark.parametrize("name", NORM_ROPE_CASES)
+def test_rope_tables_match_reference_buffers(name):
+    d = load_norm_rope(name)
+    cos, sin = oracle.rope_tables(d["rope_rows"], d["head_dim"])
+    # Same float32 formula, but torch's pow rounds a few inv_freq entries one
+    # ulp away from numpy's; theta = pos * inv_freq carries that ulp times pos
+    # (up to ~1e-4 at position 3000).
+    assert np.abs(cos[d["positions"]] - d["cos_rows"]).max() < 2e-4
+    assert np.abs(sin[d["positions"]] - d["sin_rows"]).max() < 2e-4
+
+
+@pytest.mark.parametrize("name", NORM_ROPE_CASES)
+def test_norm_rope_store_matches_reference(name):
+    d = load_norm_rope(name)
+    cos, sin = oracle.rope_tables(d["rope_rows"], d["head_dim"])
+    cos[d["positions"]] = d["cos_rows"]  # the reference module's own buffer rows
+    sin[d["positions"]] = d["sin_rows"]
+    slots = oracle.build_slot_mapping(d["positions"], d["seq_of_token"], d["block_tables"])
+    kp, vp = d["k_pool"].copy(), d["v_pool"].copy()
+    q_out = oracle.qk_norm_rope_store(d["q"], d["k_new"], d["v_new"], d["q_norm_weight"], d["k_norm_weight"],
+                                      d["eps"], cos, sin, d["positions"], kp, vp, slots)
+    # The reference ran fp32 (a handful of roundings per element); the oracle is fp64.
+    assert np.abs(q_out - d["q_ref"]).max() < 2e-6
+    changed = np.argwhere((kp != d["k_pool"]).any(-1))
+    assert np.array_equal(changed, d["k_written_idx"])
+    assert np.abs(kp[tuple(changed.T)] - d["k_written_rows"]).max() < 2e-6
+    vidx = d["v_written_idx"]
+    assert np.array_equal(vp[vidx[:, 0], vidx[:, 1], vidx[:, 2]].view(np.uint32),
+                          d["v_written_rows"].view(np.uint32))
+    untouched = np.ones(vp.shape[:3], bool)
+    untouched[vidx[:, 0], vidx[:, 1], vidx[:, 2]] = False
+    assert np.array_equal(vp[untouched], d["v_pool"][untouched])
+
+
+def test_norm_rope_oracle_catches_a_planted_rotation_error():
+    """Rotating with cat(y2, -y1) (the wrong sign convention) in a copy of the oracle must fail."""
+    d = load_norm_rope(NORM_ROPE_CASES[0])
+    x = oracle.rms_norm(d["q"], d["q_norm_weight"], d["eps"])
+    half = x.shape[-1] // 2
+    c = d["cos_rows"][:, None, :].astype(np.float64)
+    s = d["sin_rows"][:, None, :].astype(np.float64)
+    bad = c * x + s * np.concatenate([x[..., half:], -x[..., :half]], axis=-1)
+    assert np.abs(bad.transpose(1, 0, 2) - d["q_ref"]).max() > 1e-2
