@@ -420,7 +420,7 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     if args.workload in ("prefill", "qk_norm_rope"):
-        batch = workloads.config3(seed=3 + rank)
+        batch = workloads.config3(seed=3 + rank, num_seqs=args.num_seqs if args.num_seqs != 256 else 64)
     elif args.workload == "mixed":
         batch = workloads.config4(seed=4 + rank)
     else:

@@ -200,6 +200,7 @@ int fvb_qk_norm_rope_store(const void* q, int64_t q_token_stride, int64_t q_head
       v_head_stride < 0 || !(eps >= 0.f) || eps > 1.f)
     return FVB_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return FVB_OK;
+  if (num_tokens * (n_heads + 2 * int64_t(n_kv_heads)) >= (int64_t(1) << 31)) return FVB_ERR_INVALID_ARGUMENT;
   if (!q || !k || !v || !q_norm_weight || !k_norm_weight || !rope_cos || !rope_sin || !positions || !slot_mapping ||
       !q_out || !k_pool || !v_pool)
     return FVB_ERR_INVALID_ARGUMENT;

@@ -25,7 +25,8 @@
 // those lanes by xor shuffles, and the rotary partner half (d +- D/2) lives
 // in the lane half a row away, one more xor shuffle.  HBM-bound:
 // (Hq + 2 Hkv) D sizeof(T) bytes read and written per token, plus 12 bytes
-// of position / slot and the cos / sin rows (L2-resident).
+// of position / slot and the cos / sin rows (L2-resident).  The arithmetic is
+// in packed fp32x2 (FFMA2 / FMUL2) to keep the issue rate below the memory rate.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -63,92 +64,142 @@ __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret
 
 constexpr int kThreads = 256;
 
-// Row r of the launch = (token r / units, unit r % units); unit u < Hq is a
-// query head, u < Hq + Hkv a key head, the rest value heads.
+// Work split.  A row is one head of one token; a block has S = kThreads / L
+// row slots.  With units = Hq + 2 Hkv heads per token, a block takes
+// S / units whole tokens per pass when units <= S (slot j -> token j / units,
+// head j % units), otherwise one token per pass with slot j taking heads
+// j, j + S, j + 2S, ...  Each thread's heads are fixed for the whole launch,
+// so the norm weights are loaded once, position / slot / cos / sin once per
+// token, and only the rows themselves per head.  Three CTAs per SM (80
+// registers, no spills) measured faster than four (64 registers, spills).
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads) qk_norm_rope_store_kernel(
+__global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
     const T* __restrict__ q, int64_t q_ts, int64_t q_hs, const T* __restrict__ k, int64_t k_ts, int64_t k_hs,
     const T* __restrict__ v, int64_t v_ts, int64_t v_hs, const T* __restrict__ q_w, const T* __restrict__ k_w,
     float eps, const T* __restrict__ cos_t, const T* __restrict__ sin_t, int rope_rows,
-    const int32_t* __restrict__ positions, const int64_t* __restrict__ slot_mapping, int64_t num_tokens,
+    const int32_t* __restrict__ positions, const int64_t* __restrict__ slot_mapping, int num_tokens,
     int n_heads, int n_kv_heads, T* __restrict__ q_out, T* __restrict__ k_pool, T* __restrict__ v_pool,
     int64_t num_slots, int block_size, int* __restrict__ err) {
   constexpr int E = 16 / int(sizeof(T));  // elements per lane
   constexpr int L = D / E;                // lanes per row
   constexpr int HALF = L / 2;             // lane distance of the rotary partner
+  constexpr int S = kThreads / L;         // row slots per block
   static_assert(L >= 2 && L <= 32 && 32 % L == 0, "row must tile a warp");
-  constexpr int kRowsPerBlock = kThreads / L;
+  static_assert(E % 2 == 0, "pairs of elements");
   const int units = n_heads + 2 * n_kv_heads;
-  const int64_t rows = num_tokens * units;
+  const int lane = threadIdx.x & 31;
   const int sub = threadIdx.x % L;
-  const bool first_half = sub < HALF;
+  const int j = threadIdx.x / L;
+  const bool packed = units <= S;
+  const int tpb = packed ? S / units : 1;  // tokens per block pass
+  if (packed && j >= tpb * units) return;  // spare slot (its whole row group leaves together)
+  const int tok_off = packed ? j / units : 0;
+  const int u0 = packed ? j % units : j;
+  const int ustep = packed ? units : S;  // next head of this slot (one past the end when packed)
+  const uint32_t gmask = L == 32 ? 0xffffffffu : (((1u << L) - 1u) << (lane & ~(L - 1)));
+  // rope(y) = y * cos + partner(y) * (+-sin): the sign is fixed per lane.
+  const float sgn = sub < HALF ? -1.f : 1.f;
+  const float2 sgn2 = make_float2(sgn, sgn);
   const float inv_d = 1.f / float(D);
-  // The loop bound is block-uniform, so every lane of a warp reaches the shuffles.
-  for (int64_t base = int64_t(blockIdx.x) * kRowsPerBlock; base < rows;
-       base += int64_t(gridDim.x) * kRowsPerBlock) {
-    const int64_t row = base + threadIdx.x / L;
-    const bool live = row < rows;
-    const int64_t t = live ? row / units : 0;
-    const int u = live ? int(row - t * units) : 0;
-    const int kind = u < n_heads ? 0 : (u < n_heads + n_kv_heads ? 1 : 2);  // q / k / v
-    const int h = kind == 0 ? u : (kind == 1 ? u - n_heads : u - n_heads - n_kv_heads);
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (live) {
-      const T* src = kind == 0 ? q + t * q_ts + h * q_hs : (kind == 1 ? k + t * k_ts + h * k_hs : v + t * v_ts + h * v_hs);
-      raw = ldg16(src + sub * E);
-    }
-    int64_t slot = -1;
-    if (live && kind != 0) {
-      slot = __ldg(slot_mapping + t);
-      if (slot >= num_slots) {
-        record_error(err, FVB_ERR_BAD_SLOT, int(t));
-        slot = -1;
-      }
-    }
-    int pos = 0;
-    bool rope_ok = false;
-    if (live && kind != 2) {
-      pos = __ldg(positions + t);
-      rope_ok = pos >= 0 && pos < rope_rows;
-      if (!rope_ok) record_error(err, FVB_ERR_INVALID_ARGUMENT, int(t));
-    }
-    // RMSNorm (all lanes take part in the shuffles, value rows included).
-    float x[E];
+  const uint4 wq = ldg16(q_w + sub * E), wk = ldg16(k_w + sub * E);  // unpacked where used
+
+  // Norm + rope of one q or k row held as raw[] (row-group uniform).
+  auto norm_rope = [&](const uint4& raw, const uint4& wv, const float* c, const float* sn) -> uint4 {
+    float x[E], w[E];
     unpack16<T>(raw, x);
-    float ss = 0.f;
+    unpack16<T>(wv, w);
+    float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int e = 0; e < E; ++e) ss = fmaf(x[e], x[e], ss);
-#pragma unroll
-    for (int o = HALF; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss * inv_d + eps);
-    float w[E], c[E], s[E];
-    if (kind != 2 && rope_ok) {
-      unpack16<T>(ldg16((kind == 0 ? q_w : k_w) + sub * E), w);
-      unpack16<T>(ldg16(cos_t + int64_t(pos) * D + sub * E), c);
-      unpack16<T>(ldg16(sin_t + int64_t(pos) * D + sub * E), s);
-    } else {
-#pragma unroll
-      for (int e = 0; e < E; ++e) w[e] = c[e] = s[e] = 0.f;
+    for (int e = 0; e < E; e += 2) {
+      const float2 x2 = make_float2(x[e], x[e + 1]);
+      ss2 = __ffma2_rn(x2, x2, ss2);
     }
+    float ss = ss2.x + ss2.y;
+#pragma unroll
+    for (int o = HALF; o >= 1; o >>= 1) ss += __shfl_xor_sync(gmask, ss, o);
+    const float inv = rsqrtf(ss * inv_d + eps);
+    const float2 inv2 = make_float2(inv, inv);
     float y[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) y[e] = x[e] * inv * w[e];
+    for (int e = 0; e < E; e += 2) {
+      const float2 yy = __fmul2_rn(__fmul2_rn(make_float2(x[e], x[e + 1]), inv2), make_float2(w[e], w[e + 1]));
+      y[e] = yy.x;
+      y[e + 1] = yy.y;
+    }
     float r[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float yp = __shfl_xor_sync(0xffffffffu, y[e], HALF);
-      r[e] = fmaf(y[e], c[e], (first_half ? -yp : yp) * s[e]);
+    for (int e = 0; e < E; e += 2) {
+      const float2 yp = make_float2(__shfl_xor_sync(gmask, y[e], HALF), __shfl_xor_sync(gmask, y[e + 1], HALF));
+      const float2 rr = __ffma2_rn(make_float2(y[e], y[e + 1]), make_float2(c[e], c[e + 1]),
+                                   __fmul2_rn(yp, make_float2(sn[e], sn[e + 1])));
+      r[e] = rr.x;
+      r[e + 1] = rr.y;
     }
-    if (!live) continue;
-    if (kind == 0) {
-      if (rope_ok) {
-        *reinterpret_cast<uint4*>(q_out + (int64_t(h) * num_tokens + t) * D + sub * E) = pack16<T>(r);
+    return pack16<T>(r);
+  };
+
+  auto load_row = [&](int t, int uu) -> uint4 {
+    if (uu < n_heads) return ldg16(q + int64_t(t) * q_ts + uu * q_hs + sub * E);
+    if (uu < n_heads + n_kv_heads) return ldg16(k + int64_t(t) * k_ts + (uu - n_heads) * k_hs + sub * E);
+    return ldg16(v + int64_t(t) * v_ts + (uu - n_heads - n_kv_heads) * v_hs + sub * E);
+  };
+  const int tstride = gridDim.x * tpb;
+  int t = blockIdx.x * tpb + tok_off;
+  // position and slot of the next token are fetched one token ahead
+  int pos_n = t < num_tokens ? __ldg(positions + t) : 0;
+  int64_t slot_n = t < num_tokens ? __ldg(slot_mapping + t) : -1;
+  for (; t < num_tokens; t += tstride) {
+    const int pos = pos_n;
+    int64_t slot = slot_n;
+    // Rows first (independent of the position), then the position-dependent tables.
+    const bool has_b = u0 + ustep < units;
+    const uint4 ra = load_row(t, u0);
+    const uint4 rb = has_b ? load_row(t, u0 + ustep) : make_uint4(0, 0, 0, 0);
+    if (t + tstride < num_tokens) {
+      pos_n = __ldg(positions + t + tstride);
+      slot_n = __ldg(slot_mapping + t + tstride);
+    }
+    const bool rope_ok = pos >= 0 && pos < rope_rows;
+    float c[E], sn[E];
+    if (rope_ok) {
+      unpack16<T>(ldg16(cos_t + int64_t(pos) * D + sub * E), c);
+      unpack16<T>(ldg16(sin_t + int64_t(pos) * D + sub * E), sn);
+#pragma unroll
+      for (int e = 0; e < E; e += 2) {
+        const float2 s2 = __fmul2_rn(make_float2(sn[e], sn[e + 1]), sgn2);
+        sn[e] = s2.x;
+        sn[e + 1] = s2.y;
       }
-    } else if (slot >= 0 && (kind == 2 || rope_ok)) {
-      const int64_t blk = slot / block_size;
-      const int off = int(slot - blk * block_size);
-      T* dst = (kind == 1 ? k_pool : v_pool) + ((blk * n_kv_heads + h) * block_size + off) * D + sub * E;
-      *reinterpret_cast<uint4*>(dst) = kind == 1 ? pack16<T>(r) : raw;
+    }
+    if (slot >= num_slots) {
+      if (sub == 0) record_error(err, FVB_ERR_BAD_SLOT, t);
+      slot = -1;
+    }
+    if (!rope_ok && u0 == 0 && sub == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, t);
+    const int64_t blk = slot >= 0 ? slot / block_size : 0;
+    const int off = slot >= 0 ? int(slot - blk * block_size) : 0;
+    auto finish = [&](int uu, const uint4& raw) {
+      if (uu < n_heads) {
+        if (rope_ok)
+          *reinterpret_cast<uint4*>(q_out + (int64_t(uu) * num_tokens + t) * D + sub * E) = norm_rope(raw, wq, c, sn);
+      } else if (uu < n_heads + n_kv_heads) {
+        if (rope_ok && slot >= 0)
+          *reinterpret_cast<uint4*>(k_pool + ((blk * n_kv_heads + (uu - n_heads)) * block_size + off) * D + sub * E) =
+              norm_rope(raw, wk, c, sn);
+      } else if (slot >= 0) {  // value row: bit-exact copy
+        *reinterpret_cast<uint4*>(v_pool + ((blk * n_kv_heads + (uu - n_heads - n_kv_heads)) * block_size + off) * D +
+                                  sub * E) = raw;
+      }
+    };
+    finish(u0, ra);
+    if (has_b) finish(u0 + ustep, rb);
+    // Heads beyond two per slot (more than 2 S heads per token), two at a time.
+    for (int u = u0 + 2 * ustep; u < units; u += 2 * ustep) {
+      const int ub = u + ustep;
+      const uint4 xa = load_row(t, u);
+      const uint4 xb = ub < units ? load_row(t, ub) : make_uint4(0, 0, 0, 0);
+      finish(u, xa);
+      if (ub < units) finish(ub, xb);
     }
   }
 }
@@ -161,14 +212,16 @@ cudaError_t launch_typed(const void* q, int64_t q_ts, int64_t q_hs, const void* 
                          void* k_pool, void* v_pool, int64_t num_blocks, int block_size, int* err,
                          cudaStream_t stream) {
   constexpr int L = D / (16 / int(sizeof(T)));
-  const int64_t rows = num_tokens * (n_heads + 2 * n_kv_heads);
-  int64_t blocks = (rows + kThreads / L - 1) / (kThreads / L);
-  const int64_t cap = int64_t(device_sm_count()) * 8;  // 8 resident CTAs per SM, then grid-stride
+  constexpr int S = kThreads / L;
+  const int units = n_heads + 2 * n_kv_heads;
+  const int64_t tpb = units <= S ? S / units : 1;
+  int64_t blocks = (num_tokens + tpb - 1) / tpb;
+  const int64_t cap = int64_t(device_sm_count()) * 3 * 8;  // 8 waves of 3 resident CTAs per SM, then token-stride
   if (blocks > cap) blocks = cap;
   qk_norm_rope_store_kernel<T, D><<<unsigned(blocks), kThreads, 0, stream>>>(
       static_cast<const T*>(q), q_ts, q_hs, static_cast<const T*>(k), k_ts, k_hs, static_cast<const T*>(v), v_ts,
       v_hs, static_cast<const T*>(q_w), static_cast<const T*>(k_w), eps, static_cast<const T*>(cos_t),
-      static_cast<const T*>(sin_t), rope_rows, positions, slot_mapping, num_tokens, n_heads, n_kv_heads,
+      static_cast<const T*>(sin_t), rope_rows, positions, slot_mapping, int(num_tokens), n_heads, n_kv_heads,
       static_cast<T*>(q_out), static_cast<T*>(k_pool), static_cast<T*>(v_pool), num_blocks * block_size, block_size,
       err);
   return cudaGetLastError();
