@@ -318,10 +318,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seqs", type=int, default=24)
     ap.add_argument("--num-seqs", type=int, default=256, help="sequences per GPU (256 = BASELINE config 2)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long", "qk_norm_rope"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long", "qk_norm_rope", "decode_graph"],
                     help="decode = config 2 (the contract line); prefill = config 3; mixed = config 4; "
                          "long = config 5 sharded over the ranks; qk_norm_rope = the fused q/k norm + rotary + "
-                         "KV write over config 3's new tokens")
+                         "KV write over config 3's new tokens; decode_graph = one small-batch decode step "
+                         "(slots + fused norm/rope/write + attention) eager vs replayed from a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -343,6 +344,9 @@ def main():
     if world > 1:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+    if args.workload == "decode_graph":
+        run_decode_graph(args, rank, local_rank)
+        return
     if args.workload != "decode":
         run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src)
         if world > 1:
@@ -498,6 +502,72 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
             "pct_tensor_peak": round(100 * flops / (t * 1e-3) / 1e12 / (tflops_peak * world), 2),
             "pct_hbm_peak": round(100 * nbytes / (t * 1e-3) / 1e9 / (hbm_peak * world), 2),
             "peak_source": peak_src, "config": batch.name, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
+def run_decode_graph(args, rank, local_rank):
+    """Per-step latency of a small-batch decode step (config 2's heads, context U[512,4096]):
+    slot mapping + fused q/k norm / rotary / KV write + split-KV attention, launched eagerly
+    through femtovllm_b200.ops versus replayed from one captured CUDA graph."""
+    import numpy as np
+    import torch
+
+    from femtovllm_b200 import ops, workloads
+
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B = args.num_seqs if args.num_seqs != 256 else 8
+    b = workloads.config2(num_seqs=B).materialize(dev)
+    md = b.device_metadata(dev)
+    T, Hq, Hkv, D = B, b.n_heads, b.n_kv_heads, b.head_dim
+    x = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev).to(b.dtype)
+    qv, kv, vv = x[:, : Hq * D].view(T, Hq, D), x[:, Hq * D : (Hq + Hkv) * D].view(T, Hkv, D), x[:, (Hq + Hkv) * D :].view(T, Hkv, D)
+    w = torch.ones(D, device=dev, dtype=b.dtype)
+    rows = int(b.kv_lens.max()) + 1
+    inv = 1e-6 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D)
+    th = torch.arange(rows, device=dev, dtype=torch.float32)[:, None] * inv[None]
+    th = torch.cat([th, th], -1)
+    cos, sin = th.cos().to(b.dtype), th.sin().to(b.dtype)
+    pos = (md["kv_lens"] - 1).contiguous()
+
+    def step():
+        slots = ops.build_slot_mapping(pos, md["block_tables"])
+        q_hm = ops.qk_norm_rope_store(qv, kv, vv, w, w, 1e-6, cos, sin, pos, b.k_pool, b.v_pool, slots)
+        return ops.paged_attention_gemv(q_hm, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps * 1e3
+
+    eager_us = timed(step)
+    graph_us = timed(g.replay)
+    del g
+    line = {"metric": "decode step latency (us), eager vs CUDA graph", "workload": "decode_graph", "num_seqs": B,
+            "n_heads": Hq, "n_kv_heads": Hkv, "head_dim": D, "kv_len": "U[512,4096]", "steps": args.steps,
+            "eager_us": round(eager_us, 2), "graph_us": round(graph_us, 2),
+            "speedup": round(eager_us / graph_us, 2), "kv_bytes": int(b.decode_bytes()),
+            "graph_gbs": round(b.decode_bytes() / (graph_us * 1e-6) / 1e9, 1),
+            "launches_per_step": 4, "data": "synthetic (seeded)"}
     print(json.dumps(line), flush=True)
 
 
