@@ -101,6 +101,27 @@ FVB_API int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens,
                                    int block_size, int64_t* slot_mapping, void* stream);
 
 /*
+ * Varlen attention metadata from per-sequence counts, on the device.  For sequence s with
+ * num_computed[s] cached and num_new[s] new tokens (decode: num_new[s] = 1):
+ *   cu_seqlens[s + 1] = num_new[0] + ... + num_new[s], cu_seqlens[0] = 0          (num_seqs + 1 entries)
+ *   kv_lens[s] = num_computed[s] + num_new[s]                                      (num_seqs entries)
+ *   positions[t] = num_computed[s] + t - cu_seqlens[s] for each new token t of s   (num_tokens entries)
+ *   block_tables[s][i] = flat_blocks[cu_blocks[s] + i] for i < cu_blocks[s+1] - cu_blocks[s], else -1
+ *                                                                   (num_seqs x max_blocks_per_seq, int32)
+ *   slot_mapping[t] (optional, may be NULL) as fvb_build_slot_mapping.
+ * The host loops of ModelRunner._route_prefill / _route_decode
+ * (femtovllm/engine/model_runner.py:186-205, 280-290) and pad_block_tables (:46-72), which build these as
+ * Python lists each step.  num_tokens (the sum of num_new) and max_blocks_per_seq (the widest row) are the
+ * caller's, as the scheduler knows them; a mismatch or a malformed cu_blocks row is recorded in the device
+ * error word (FVB_ERR_INVALID_ARGUMENT) and never read out of bounds.  Two launches, no host synchronization.
+ */
+FVB_API int fvb_build_varlen_metadata(const int32_t* num_computed, const int32_t* num_new, int num_seqs,
+                                      const int32_t* flat_blocks, int64_t num_flat_blocks,
+                                      const int32_t* cu_blocks, int max_blocks_per_seq, int64_t num_tokens,
+                                      int32_t* positions, int32_t* cu_seqlens, int32_t* kv_lens,
+                                      int32_t* block_tables, int64_t* slot_mapping, void* stream);
+
+/*
  * Fused q/k RMSNorm + rotary embedding + KV-cache write, one pass over the projection outputs:
  *   q_out[h][t][:]                      = rope(rmsnorm(q[t][h][:]) * q_norm_weight)
  *   k_pool[slot / 16][h][slot % 16][:]  = rope(rmsnorm(k[t][h][:]) * k_norm_weight)
@@ -143,6 +164,31 @@ FVB_API int fvb_paged_attention_decode(const void* q, void* out, const void* k_p
                                int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
                                const int32_t* kv_lens, int max_kv_len, int dtype, void* workspace,
                                size_t workspace_bytes, void* stream);
+
+/*
+ * fvb_paged_attention_decode / _prefill with q and out at any (token, head) strides, in elements:
+ * element (t, h, d) of q is q[t * q_token_stride + h * q_head_stride + d], likewise for out.  The reference
+ * op layout (n_heads, T, D) is strides (D, T * D); the projection / o_proj layout (T, n_heads, D) is
+ * (n_heads * D, D).  With the latter, the copies the reference makes around the op (q.transpose(0, 1) +
+ * .contiguous(), femtovllm/ops/__init__.py:41-42; attn.transpose(0, 1).contiguous() before o_proj,
+ * femtovllm/models/qwen/qwen3.py:278, 385) are not needed.  Every stride times the element size must be a
+ * multiple of 16 bytes.  Workspace sizes as for the unstrided entry points.
+ */
+FVB_API int fvb_paged_attention_decode_strided(const void* q, int64_t q_token_stride, int64_t q_head_stride,
+                                               void* out, int64_t out_token_stride, int64_t out_head_stride,
+                                               const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                               int n_heads, int n_kv_heads, int head_dim, int block_size,
+                                               int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
+                                               const int32_t* kv_lens, int max_kv_len, int dtype, void* workspace,
+                                               size_t workspace_bytes, void* stream);
+FVB_API int fvb_paged_attention_prefill_strided(const void* q, int64_t q_token_stride, int64_t q_head_stride,
+                                                void* out, int64_t out_token_stride, int64_t out_head_stride,
+                                                const void* k_pool, const void* v_pool, int64_t num_blocks,
+                                                int n_heads, int n_kv_heads, int head_dim, int block_size,
+                                                int num_seqs, int64_t q_len_flatten, const int32_t* cu_seqlens,
+                                                int max_q_len, const int32_t* block_tables, int max_blocks_per_seq,
+                                                const int32_t* kv_lens, const int32_t* positions, int dtype,
+                                                void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Decode paged attention without a caller-provided workspace.  No counterpart

@@ -80,6 +80,18 @@ int check_attention(const void* q, const void* out, const void* k_pool, const vo
   return FVB_OK;
 }
 
+// q / out strides (elements): non-negative, and every row start 16-byte aligned
+// (the tensor-core prefill loads q rows with TMA and stores out rows as 16-byte vectors).
+int check_layout(const QOLayout& lay, int dtype) {
+  const int64_t es = esize_of(dtype);
+  const int64_t st[4] = {lay.q_ts, lay.q_hs, lay.o_ts, lay.o_hs};
+  for (int64_t x : st) {
+    if (x < 0) return FVB_ERR_INVALID_ARGUMENT;
+    if ((x * es) % 16 != 0) return FVB_ERR_MISALIGNED;
+  }
+  return FVB_OK;
+}
+
 }  // namespace
 
 int device_sm_count() {
@@ -92,8 +104,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-cudaError_t make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
-                        uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+namespace {
+cudaError_t tensor_map_encoder(EncodeTiledFn* out) {
   static EncodeTiledFn encode = nullptr;
   if (!encode) {
     void* fn = nullptr;
@@ -103,11 +115,36 @@ cudaError_t make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
     if (qres != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
     encode = reinterpret_cast<EncodeTiledFn>(fn);
   }
+  *out = encode;
+  return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols, uint64_t rows,
+                        uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+  EncodeTiledFn encode = nullptr;
+  cudaError_t e = tensor_map_encoder(&encode);
+  if (e != cudaSuccess) return e;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t make_tma_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, const uint64_t dims3[3],
+                        const uint64_t stride_bytes[2], const uint32_t box3[3], bool swizzle128) {
+  EncodeTiledFn encode = nullptr;
+  cudaError_t e = tensor_map_encoder(&encode);
+  if (e != cudaSuccess) return e;
+  const cuuint64_t dims[3] = {dims3[0], dims3[1], dims3[2]};
+  const cuuint64_t strides[2] = {stride_bytes[0], stride_bytes[1]};
+  const cuuint32_t box[3] = {box3[0], box3[1], box3[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
@@ -185,6 +222,27 @@ int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_
                                           static_cast<cudaStream_t>(stream)));
 }
 
+int fvb_build_varlen_metadata(const int32_t* num_computed, const int32_t* num_new, int num_seqs,
+                              const int32_t* flat_blocks, int64_t num_flat_blocks, const int32_t* cu_blocks,
+                              int max_blocks_per_seq, int64_t num_tokens, int32_t* positions, int32_t* cu_seqlens,
+                              int32_t* kv_lens, int32_t* block_tables, int64_t* slot_mapping, void* stream) {
+  if (num_seqs <= 0 || num_tokens < 0 || max_blocks_per_seq < 0 || num_flat_blocks < 0 ||
+      num_tokens >= (int64_t(1) << 31))
+    return FVB_ERR_INVALID_ARGUMENT;
+  if (!num_computed || !num_new || !cu_blocks || !cu_seqlens || !kv_lens) return FVB_ERR_INVALID_ARGUMENT;
+  if (num_tokens > 0 && !positions) return FVB_ERR_INVALID_ARGUMENT;
+  if (max_blocks_per_seq > 0 && !block_tables) return FVB_ERR_INVALID_ARGUMENT;
+  if (num_flat_blocks > 0 && !flat_blocks) return FVB_ERR_INVALID_ARGUMENT;
+  if (slot_mapping && (reinterpret_cast<uintptr_t>(slot_mapping) & 7) != 0) return FVB_ERR_MISALIGNED;
+  cudaError_t e;
+  int* err = device_error_ptr(&e);
+  if (!err) return cuda_status(e);
+  return cuda_status(launch_build_varlen_metadata(num_computed, num_new, num_seqs, flat_blocks, num_flat_blocks,
+                                                  cu_blocks, max_blocks_per_seq, num_tokens, positions, cu_seqlens,
+                                                  kv_lens, block_tables, slot_mapping, err,
+                                                  static_cast<cudaStream_t>(stream)));
+}
+
 int fvb_qk_norm_rope_store(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
                            int64_t k_token_stride, int64_t k_head_stride, const void* v, int64_t v_token_stride,
                            int64_t v_head_stride, const void* q_norm_weight, const void* k_norm_weight, float eps,
@@ -251,8 +309,24 @@ int fvb_paged_attention_decode(const void* q, void* out, const void* k_pool, con
                                int n_heads, int n_kv_heads, int head_dim, int block_size, int num_seqs,
                                const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
                                int max_kv_len, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  const QOLayout lay = head_major_layout(num_seqs, head_dim);
+  return fvb_paged_attention_decode_strided(q, lay.q_ts, lay.q_hs, out, lay.o_ts, lay.o_hs, k_pool, v_pool,
+                                            num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
+                                            block_tables, max_blocks_per_seq, kv_lens, max_kv_len, dtype, workspace,
+                                            workspace_bytes, stream);
+}
+
+int fvb_paged_attention_decode_strided(const void* q, int64_t q_token_stride, int64_t q_head_stride, void* out,
+                                       int64_t out_token_stride, int64_t out_head_stride, const void* k_pool,
+                                       const void* v_pool, int64_t num_blocks, int n_heads, int n_kv_heads,
+                                       int head_dim, int block_size, int num_seqs, const int32_t* block_tables,
+                                       int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_attention(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
                            block_tables, max_blocks_per_seq, kv_lens, dtype);
+  if (st) return st;
+  const QOLayout lay{q_token_stride, q_head_stride, out_token_stride, out_head_stride};
+  st = check_layout(lay, dtype);
   if (st) return st;
   if (num_seqs == 0) return FVB_OK;
   if (max_kv_len < 0 || int64_t(max_kv_len) > int64_t(max_blocks_per_seq) * kPageSize) return FVB_ERR_INVALID_ARGUMENT;
@@ -263,8 +337,8 @@ int fvb_paged_attention_decode(const void* q, void* out, const void* k_pool, con
   int* err = device_error_ptr(&e);
   if (!err) return cuda_status(e);
   return cuda_status(launch_decode(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
-                                   block_tables, max_blocks_per_seq, kv_lens, max_kv_len, dtype, plan, workspace, err,
-                                   static_cast<cudaStream_t>(stream)));
+                                   block_tables, max_blocks_per_seq, kv_lens, max_kv_len, dtype, plan, lay, workspace,
+                                   err, static_cast<cudaStream_t>(stream)));
 }
 
 size_t fvb_paged_attention_prefill_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
@@ -281,27 +355,44 @@ int fvb_paged_attention_prefill(const void* q, void* out, const void* k_pool, co
                                 const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
                                 const int32_t* positions, int dtype, void* workspace, size_t workspace_bytes,
                                 void* stream) {
+  const QOLayout lay = head_major_layout(q_len_flatten, head_dim);
+  return fvb_paged_attention_prefill_strided(q, lay.q_ts, lay.q_hs, out, lay.o_ts, lay.o_hs, k_pool, v_pool,
+                                             num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
+                                             q_len_flatten, cu_seqlens, max_q_len, block_tables, max_blocks_per_seq,
+                                             kv_lens, positions, dtype, workspace, workspace_bytes, stream);
+}
+
+int fvb_paged_attention_prefill_strided(const void* q, int64_t q_token_stride, int64_t q_head_stride, void* out,
+                                        int64_t out_token_stride, int64_t out_head_stride, const void* k_pool,
+                                        const void* v_pool, int64_t num_blocks, int n_heads, int n_kv_heads,
+                                        int head_dim, int block_size, int num_seqs, int64_t q_len_flatten,
+                                        const int32_t* cu_seqlens, int max_q_len, const int32_t* block_tables,
+                                        int max_blocks_per_seq, const int32_t* kv_lens, const int32_t* positions,
+                                        int dtype, void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_attention(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
                            block_tables, max_blocks_per_seq, kv_lens, dtype);
+  if (st) return st;
+  const QOLayout lay{q_token_stride, q_head_stride, out_token_stride, out_head_stride};
+  st = check_layout(lay, dtype);
   if (st) return st;
   if (q_len_flatten < 0 || max_q_len < 0) return FVB_ERR_INVALID_ARGUMENT;
   if (num_seqs == 0 || q_len_flatten == 0) return FVB_OK;
   if (!cu_seqlens || !positions) return FVB_ERR_INVALID_ARGUMENT;
-  if (q_len_flatten * n_heads > int64_t(0x7fffffff)) return FVB_ERR_UNSUPPORTED;  // TMA row coordinate of q
+  if (q_len_flatten > int64_t(0x7fffffff)) return FVB_ERR_UNSUPPORTED;  // TMA token coordinate of q
   cudaError_t e;
   int* err = device_error_ptr(&e);
   if (!err) return cuda_status(e);
   if (dtype == FVB_DTYPE_F32) {
     return cuda_status(launch_prefill_simt(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim,
                                            num_seqs, q_len_flatten, cu_seqlens, block_tables, max_blocks_per_seq,
-                                           kv_lens, positions, dtype, err, static_cast<cudaStream_t>(stream)));
+                                           kv_lens, positions, dtype, lay, err, static_cast<cudaStream_t>(stream)));
   }
   const PrefillPlan plan = plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, q_len_flatten, max_q_len, dtype);
   if (!workspace || workspace_bytes < plan.ws_bytes) return FVB_ERR_WORKSPACE_TOO_SMALL;
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return FVB_ERR_MISALIGNED;
   return cuda_status(launch_prefill(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
                                     q_len_flatten, cu_seqlens, max_q_len, block_tables, max_blocks_per_seq, kv_lens,
-                                    positions, dtype, plan, workspace, err, static_cast<cudaStream_t>(stream)));
+                                    positions, dtype, plan, lay, workspace, err, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     const uint8_t* __restrict__ v_pool, int64_t num_blocks, int n_kv_heads, int num_seqs,
     const int32_t* __restrict__ block_tables, int max_blocks_per_seq, const int32_t* __restrict__ kv_lens,
     int kv_cap, int pages_per_split, int max_splits, float* __restrict__ ws_o, float* __restrict__ ws_lse,
-    int* __restrict__ err) {
+    const QOLayout lay, int* __restrict__ err) {
   using Tr = DecodeTraits<T, D, NREP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     if (split == 0) {
       for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
         const int r = e / D, d = e % D;
-        out[(int64_t(kvh * NREP + r) * num_seqs + b) * D + d] = Elem<T>::from_f(0.f);
+        out[int64_t(b) * lay.o_ts + int64_t(kvh * NREP + r) * lay.o_hs + d] = Elem<T>::from_f(0.f);
       }
     }
     return;
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     const float scale = kLog2e * rsqrtf(float(D));
     for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
       const int r = e / D, d = e % D;
-      qs[e] = Elem<T>::to_f(q[(int64_t(kvh * NREP + r) * num_seqs + b) * D + d]) * scale;
+      qs[e] = Elem<T>::to_f(q[int64_t(b) * lay.q_ts + int64_t(kvh * NREP + r) * lay.q_hs + d]) * scale;
     }
   }
   __syncthreads();
@@ -325,7 +325,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     }
     const int head = kvh * NREP + r;
     if (nsplits == 1) {
-      out[(int64_t(head) * num_seqs + b) * D + d] = Elem<T>::from_f(O / L);
+      out[int64_t(b) * lay.o_ts + int64_t(head) * lay.o_hs + d] = Elem<T>::from_f(O / L);
     } else {
       const int64_t idx = (int64_t(b) * n_heads + head) * max_splits + split;
       ws_o[idx * D + d] = O / L;
@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restri
                                                            const float* __restrict__ ws_lse, T* __restrict__ out,
                                                            const int32_t* __restrict__ kv_lens, int kv_cap,
                                                            int num_seqs, int n_heads, int pages_per_split,
-                                                           int max_splits) {
+                                                           int max_splits, const QOLayout lay) {
   extern __shared__ float wsh[];  // [max_splits] weights, then [D / 32] partial maxima / sums
   float* red = wsh + max_splits;
   const int b = blockIdx.x / n_heads, head = blockIdx.x % n_heads;
@@ -388,14 +388,14 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restri
     o3 = fmaf(wsh[s + 3], __ldg(src + int64_t(s + 3) * D), o3);
   }
   for (; s < nsplits; ++s) o0 = fmaf(wsh[s], __ldg(src + int64_t(s) * D), o0);
-  out[(int64_t(head) * num_seqs + b) * D + d] = Elem<T>::from_f(((o0 + o1) + (o2 + o3)) / L);
+  out[int64_t(b) * lay.o_ts + int64_t(head) * lay.o_hs + d] = Elem<T>::from_f(((o0 + o1) + (o2 + o3)) / L);
 }
 
 template <typename T, int D, int NREP>
 cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                             int n_kv_heads, int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
-                            const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan, void* workspace,
-                            int* err, cudaStream_t stream) {
+                            const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan, const QOLayout& lay,
+                            void* workspace, int* err, cudaStream_t stream) {
   using Tr = DecodeTraits<T, D, NREP>;
   const int kv_cap = int(std::min<int64_t>(std::min<int64_t>(max_kv_len, int64_t(max_blocks_per_seq) * kPageSize),
                                            int64_t(plan.max_splits) * plan.pages_per_split * kPageSize));
@@ -420,7 +420,7 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
   kern<<<grid, kDecodeThreads, Tr::kSmemBytes, stream>>>(
       kmap, static_cast<const T*>(q), static_cast<T*>(out), static_cast<const uint8_t*>(v_pool), num_blocks,
       n_kv_heads, num_seqs, block_tables, max_blocks_per_seq, kv_lens, kv_cap, plan.pages_per_split, plan.max_splits,
-      ws_o, ws_lse, err);
+      ws_o, ws_lse, lay, err);
   ce = cudaGetLastError();
   if (ce != cudaSuccess || plan.max_splits <= 1) return ce;
   const size_t csmem = (size_t(plan.max_splits) + D / 32) * sizeof(float);
@@ -430,7 +430,7 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
   }
   decode_combine_kernel<T, D><<<unsigned(num_seqs * n_kv_heads * NREP), D, csmem, stream>>>(
       ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap, num_seqs, n_kv_heads * NREP, plan.pages_per_split,
-      plan.max_splits);
+      plan.max_splits, lay);
   return cudaGetLastError();
 }
 
@@ -438,20 +438,20 @@ template <typename T, int D>
 cudaError_t dispatch_nrep(int nrep, const void* q, void* out, const void* k_pool, const void* v_pool,
                           int64_t num_blocks, int n_kv_heads, int num_seqs, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan,
-                          void* ws, int* err, cudaStream_t stream) {
+                          const QOLayout& lay, void* ws, int* err, cudaStream_t stream) {
   switch (nrep) {
     case 1:
       return launch_decode_t<T, D, 1>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
     case 2:
       return launch_decode_t<T, D, 2>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
     case 4:
       return launch_decode_t<T, D, 4>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
     case 8:
       return launch_decode_t<T, D, 8>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, ws, err, stream);
+                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -484,11 +484,12 @@ DecodePlan plan_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, 
 cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                           int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
-                          const DecodePlan& plan, void* workspace, int* err, cudaStream_t stream) {
+                          const DecodePlan& plan, const QOLayout& lay, void* workspace, int* err,
+                          cudaStream_t stream) {
   if (num_seqs == 0) return cudaSuccess;
   const int nrep = n_heads / n_kv_heads;
 #define FVB_DECODE_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables, \
-                        max_blocks_per_seq, kv_lens, max_kv_len, plan, workspace, err, stream
+                        max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, workspace, err, stream
   if (dtype == FVB_DTYPE_BF16) {
     return head_dim == 128 ? dispatch_nrep<__nv_bfloat16, 128>(FVB_DECODE_ARGS)
                            : dispatch_nrep<__nv_bfloat16, 64>(FVB_DECODE_ARGS);

@@ -15,6 +15,21 @@ namespace fvb {
 cudaError_t make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t cols,
                         uint64_t rows, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128);
 
+// The same encoder for a 3-D box: dims {d0, d1, d2} elements, byte strides of
+// dims 1 and 2 (multiples of 16, in any order), box {b0, b1, b2}.
+cudaError_t make_tma_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, const uint64_t dims[3],
+                        const uint64_t stride_bytes[2], const uint32_t box[3], bool swizzle128);
+
+// Where q and out live: element (token t, head h, d) at t * ts + h * hs + d.
+// Head-major (n_heads, T, D), the reference op layout, is {D, T * D}; the
+// projection / o_proj layout (T, n_heads, D) is {n_heads * D, D}.
+struct QOLayout {
+  int64_t q_ts, q_hs, o_ts, o_hs;
+};
+inline QOLayout head_major_layout(int64_t tokens, int head_dim) {
+  return QOLayout{head_dim, tokens * head_dim, head_dim, tokens * head_dim};
+}
+
 cudaError_t launch_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride,
                                  void* k_pool, void* v_pool, int64_t num_blocks, const int64_t* slot_mapping,
                                  int64_t num_tokens, int n_kv_heads, int head_dim, int block_size, int esize,
@@ -36,7 +51,8 @@ DecodePlan plan_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, 
 cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                           int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
-                          const DecodePlan& plan, void* workspace, int* err, cudaStream_t stream);
+                          const DecodePlan& plan, const QOLayout& lay, void* workspace, int* err,
+                          cudaStream_t stream);
 
 struct PrefillPlan {
   int tile_tokens;      // query tokens per tile (128 / GQA group on the tensor-core path)
@@ -50,13 +66,14 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
                            int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,
                            const int32_t* cu_seqlens, int max_q_len, const int32_t* block_tables,
                            int max_blocks_per_seq, const int32_t* kv_lens, const int32_t* positions, int dtype,
-                           const PrefillPlan& plan, void* workspace, int* err, cudaStream_t stream);
+                           const PrefillPlan& plan, const QOLayout& lay, void* workspace, int* err,
+                           cudaStream_t stream);
 
 cudaError_t launch_prefill_simt(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                                 int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,
                                 const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
-                                const int32_t* kv_lens, const int32_t* positions, int dtype, int* err,
-                                cudaStream_t stream);
+                                const int32_t* kv_lens, const int32_t* positions, int dtype, const QOLayout& lay,
+                                int* err, cudaStream_t stream);
 
 // Fused q/k RMSNorm + rotary embedding + K/V pool write (qk_norm_rope.cu).
 // Strides are in elements; q_out is [n_heads][num_tokens][head_dim].
@@ -67,6 +84,13 @@ cudaError_t launch_qk_norm_rope_store(const void* q, int64_t q_ts, int64_t q_hs,
                                       int n_heads, int n_kv_heads, int head_dim, void* q_out, void* k_pool,
                                       void* v_pool, int64_t num_blocks, int block_size, int dtype, int* err,
                                       cudaStream_t stream);
+
+// Varlen metadata from per-sequence counts (metadata.cu); slot_mapping may be null.
+cudaError_t launch_build_varlen_metadata(const int32_t* num_computed, const int32_t* num_new, int num_seqs,
+                                         const int32_t* flat_blocks, int64_t num_flat_blocks, const int32_t* cu_blocks,
+                                         int max_blocks_per_seq, int64_t num_tokens, int32_t* positions,
+                                         int32_t* cu_seqlens, int32_t* kv_lens, int32_t* block_tables,
+                                         int64_t* slot_mapping, int* err, cudaStream_t stream);
 
 int device_sm_count();
 

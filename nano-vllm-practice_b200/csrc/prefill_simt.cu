@@ -36,7 +36,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) prefill_simt_kernel(
     const T* __restrict__ q, T* __restrict__ out, const T* __restrict__ k_pool, const T* __restrict__ v_pool,
     int64_t num_blocks, int n_heads, int n_kv_heads, int num_seqs, int64_t q_len_flatten,
     const int32_t* __restrict__ cu_seqlens, const int32_t* __restrict__ block_tables, int max_blocks_per_seq,
-    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, int* __restrict__ err) {
+    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, const QOLayout lay,
+    int* __restrict__ err) {
   constexpr int kDPL = D / 32;
   __shared__ float qsh[kWarpsPerCta][D];
   __shared__ float psh[kWarpsPerCta][32];
@@ -61,7 +62,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) prefill_simt_kernel(
   const int pos = __ldg(positions + tok);
   const int n_keys = min(kv_len, pos + 1);
   const float scale = kLog2e * rsqrtf(float(D));
-  for (int d = lane; d < D; d += 32) qsh[warp][d] = Elem<T>::to_f(q[row * D + d]) * scale;
+  const T* qrow = q + tok * lay.q_ts + int64_t(head) * lay.q_hs;
+  for (int d = lane; d < D; d += 32) qsh[warp][d] = Elem<T>::to_f(qrow[d]) * scale;
   __syncwarp();
   const int32_t* table = block_tables + int64_t(s) * max_blocks_per_seq;
   float m = -INFINITY, l = 0.f, acc[kDPL];
@@ -105,14 +107,16 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) prefill_simt_kernel(
   }
   const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-  for (int i = 0; i < kDPL; ++i) out[row * D + lane * kDPL + i] = Elem<T>::from_f(acc[i] * inv);
+  T* orow = out + tok * lay.o_ts + int64_t(head) * lay.o_hs;
+  for (int i = 0; i < kDPL; ++i) orow[lane * kDPL + i] = Elem<T>::from_f(acc[i] * inv);
 }
 
 template <typename T>
 cudaError_t launch_simt_t(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                           int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,
                           const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
-                          const int32_t* kv_lens, const int32_t* positions, int* err, cudaStream_t stream) {
+                          const int32_t* kv_lens, const int32_t* positions, const QOLayout& lay, int* err,
+                          cudaStream_t stream) {
   const int64_t rows = int64_t(n_heads) * q_len_flatten;
   const int64_t blocks = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
   if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
@@ -120,7 +124,7 @@ cudaError_t launch_simt_t(const void* q, void* out, const void* k_pool, const vo
     kern<<<unsigned(blocks), 32 * kWarpsPerCta, 0, stream>>>(
         static_cast<const T*>(q), static_cast<T*>(out), static_cast<const T*>(k_pool),
         static_cast<const T*>(v_pool), num_blocks, n_heads, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens,
-        block_tables, max_blocks_per_seq, kv_lens, positions, err);
+        block_tables, max_blocks_per_seq, kv_lens, positions, lay, err);
   };
   if (head_dim == 128) args(prefill_simt_kernel<T, 128>);
   else args(prefill_simt_kernel<T, 64>);
@@ -132,22 +136,22 @@ cudaError_t launch_simt_t(const void* q, void* out, const void* k_pool, const vo
 cudaError_t launch_prefill_simt(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                                 int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,
                                 const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
-                                const int32_t* kv_lens, const int32_t* positions, int dtype, int* err,
-                                cudaStream_t stream) {
+                                const int32_t* kv_lens, const int32_t* positions, int dtype, const QOLayout& lay,
+                                int* err, cudaStream_t stream) {
   if (q_len_flatten == 0 || num_seqs == 0) return cudaSuccess;
   switch (dtype) {
     case FVB_DTYPE_BF16:
       return launch_simt_t<__nv_bfloat16>(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim,
                                           num_seqs, q_len_flatten, cu_seqlens, block_tables, max_blocks_per_seq,
-                                          kv_lens, positions, err, stream);
+                                          kv_lens, positions, lay, err, stream);
     case FVB_DTYPE_F16:
       return launch_simt_t<__half>(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
                                    q_len_flatten, cu_seqlens, block_tables, max_blocks_per_seq, kv_lens,
-                                   positions, err, stream);
+                                   positions, lay, err, stream);
     default:
       return launch_simt_t<float>(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
                                   q_len_flatten, cu_seqlens, block_tables, max_blocks_per_seq, kv_lens, positions,
-                                  err, stream);
+                                  lay, err, stream);
   }
 }
 

@@ -177,7 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     const __grid_constant__ CUtensorMap vmap, T* __restrict__ out, int64_t q_len_flatten, int num_seqs,
     int n_kv_heads, int64_t num_blocks, const int32_t* __restrict__ cu_seqlens, const int32_t* __restrict__ order,
     const int32_t* __restrict__ cu_items, const int32_t* __restrict__ block_tables, int max_blocks_per_seq,
-    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, int* __restrict__ err) {
+    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, const QOLayout lay,
+    int* __restrict__ err) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;  // query tokens per tile
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     for (int e = threadIdx.x; e < 2 * kTileM * D; e += kThreads) {
       const int i = e / (kTileM * D), r = (e / D) % kTileM, tok = t0[i] + r % TOK;
       if ((i == 0 || has1) && tok <= t_last[i])
-        out[(int64_t(kvh * NREP + r / TOK) * q_len_flatten + tok) * D + e % D] = Elem<T>::from_f(0.f);
+        out[int64_t(tok) * lay.o_ts + int64_t(kvh * NREP + r / TOK) * lay.o_hs + e % D] = Elem<T>::from_f(0.f);
     }
     return;
   }
@@ -273,11 +274,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
         for (int i = 0; i < (has1 ? 2 : 1); ++i) {
 #pragma unroll
           for (int g = 0; g < NREP; ++g) {
-            const int row = int((int64_t(kvh) * NREP + g) * q_len_flatten + t0[i]);
 #pragma unroll
             for (int h = 0; h < C::kHalves; ++h) {
-              tma_load_2d(smem + C::kOffQ + i * C::kQTileBytes + h * kHalfBytes + g * TOK * 128, &qmap, h * 64, row,
-                          q_full);
+              // box = TOK tokens x 64 dims of head kvh * NREP + g (rows past the end read as zeros)
+              tma_load_3d(smem + C::kOffQ + i * C::kQTileBytes + h * kHalfBytes + g * TOK * 128, &qmap, h * 64, t0[i],
+                          kvh * NREP + g, q_full);
             }
           }
         }
@@ -512,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.f / l;
-      T* orow = out + (int64_t(head) * q_len_flatten + tok) * D;
+      T* orow = out + int64_t(tok) * lay.o_ts + int64_t(head) * lay.o_hs;
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t o[32];
@@ -545,15 +546,19 @@ template <typename T, int D, int NREP>
 cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                       int n_kv_heads, int num_seqs, int64_t q_len_flatten, const int32_t* cu_seqlens,
                       const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
-                      const int32_t* positions, const PrefillPlan& plan, void* workspace, int* err,
-                      cudaStream_t stream) {
+                      const int32_t* positions, const PrefillPlan& plan, const QOLayout& lay, void* workspace,
+                      int* err, cudaStream_t stream) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;
   const CUtensorMapDataType tdt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap qmap, kmap, vmap;
   const uint64_t pool_rows = uint64_t(num_blocks) * n_kv_heads * kPageSize;
-  cudaError_t ce = make_tma_2d(&qmap, q, tdt, D, uint64_t(n_kv_heads) * NREP * q_len_flatten, D * 2, 64, TOK, true);
+  // q as (D, tokens, heads) with the caller's strides: any (T, H, D)-indexable layout.
+  const uint64_t qdims[3] = {uint64_t(D), uint64_t(q_len_flatten), uint64_t(n_kv_heads) * NREP};
+  const uint64_t qstrides[2] = {uint64_t(lay.q_ts) * 2, uint64_t(lay.q_hs) * 2};
+  const uint32_t qbox[3] = {64, uint32_t(TOK), 1};
+  cudaError_t ce = make_tma_3d(&qmap, q, tdt, qdims, qstrides, qbox, true);
   if (ce == cudaSuccess) ce = make_tma_2d(&kmap, k_pool, tdt, D, pool_rows, D * 2, 64, kPageSize, true);
   if (ce == cudaSuccess) ce = make_tma_2d(&vmap, v_pool, tdt, D, pool_rows, D * 2, 64, kPageSize, true);
   if (ce != cudaSuccess) return ce;
@@ -569,8 +574,8 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
   kern<<<unsigned(ctas), kThreads, C::kSmemBytes, stream>>>(qmap, kmap, vmap, static_cast<T*>(out), q_len_flatten,
                                                             num_seqs, n_kv_heads, num_blocks, cu_seqlens, order,
-                                                            cu_items, block_tables,
-                                                  max_blocks_per_seq, kv_lens, positions, err);
+                                                            cu_items, block_tables, max_blocks_per_seq, kv_lens,
+                                                            positions, lay, err);
   return cudaGetLastError();
 }
 
@@ -578,10 +583,10 @@ template <typename T, int D>
 cudaError_t dispatch_tc(int nrep, const void* q, void* out, const void* k_pool, const void* v_pool,
                         int64_t num_blocks, int n_kv_heads, int num_seqs, int64_t q_len_flatten,
                         const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
-                        const int32_t* kv_lens, const int32_t* positions, const PrefillPlan& plan, void* ws, int* err,
-                        cudaStream_t stream) {
+                        const int32_t* kv_lens, const int32_t* positions, const PrefillPlan& plan,
+                        const QOLayout& lay, void* ws, int* err, cudaStream_t stream) {
 #define FVB_TC_ARGS q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, block_tables, \
-                    max_blocks_per_seq, kv_lens, positions, plan, ws, err, stream
+                    max_blocks_per_seq, kv_lens, positions, plan, lay, ws, err, stream
   switch (nrep) {
     case 1:
       return launch_tc<T, D, 1>(FVB_TC_ARGS);
@@ -622,12 +627,13 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
                            int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,
                            const int32_t* cu_seqlens, int max_q_len, const int32_t* block_tables,
                            int max_blocks_per_seq, const int32_t* kv_lens, const int32_t* positions, int dtype,
-                           const PrefillPlan& plan, void* workspace, int* err, cudaStream_t stream) {
+                           const PrefillPlan& plan, const QOLayout& lay, void* workspace, int* err,
+                           cudaStream_t stream) {
   (void)max_q_len;
   if (num_seqs == 0 || q_len_flatten == 0) return cudaSuccess;
   const int nrep = n_heads / n_kv_heads;
 #define FVB_DISPATCH_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, \
-                          block_tables, max_blocks_per_seq, kv_lens, positions, plan, workspace, err, stream
+                          block_tables, max_blocks_per_seq, kv_lens, positions, plan, lay, workspace, err, stream
   if (dtype == FVB_DTYPE_BF16) {
     return head_dim == 128 ? dispatch_tc<__nv_bfloat16, 128>(FVB_DISPATCH_ARGS)
                            : dispatch_tc<__nv_bfloat16, 64>(FVB_DISPATCH_ARGS);

@@ -42,14 +42,21 @@ void check_status(int st, const char* what) {
   TORCH_CHECK(false, what, " failed: ", fvb_status_string(st));
 }
 
+// out of shape (n_heads, T, D): head-major memory, or a transposed view of a
+// (T, n_heads, D) buffer when token_major (then out.transpose(0, 1) is contiguous).
+at::Tensor new_out(const at::Tensor& q, bool token_major) {
+  if (!token_major) return torch::empty({q.size(0), q.size(1), q.size(2)}, q.options());
+  return torch::empty({q.size(1), q.size(0), q.size(2)}, q.options()).transpose(0, 1);
+}
+
 void* stream_of(const at::Tensor& t) {
   return static_cast<void*>(at::cuda::getCurrentCUDAStream(t.get_device()).stream());
 }
 
 void check_pools(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool) {
   TORCH_CHECK(q.is_cuda() && k_pool.is_cuda() && v_pool.is_cuda(), "q, k_pool and v_pool must be CUDA tensors");
-  TORCH_CHECK(q.is_contiguous() && k_pool.is_contiguous() && v_pool.is_contiguous(),
-              "q, k_pool and v_pool must be contiguous");
+  TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1, "d_head must be the contiguous dimension of q");
+  TORCH_CHECK(k_pool.is_contiguous() && v_pool.is_contiguous(), "k_pool and v_pool must be contiguous");
   TORCH_CHECK(q.dim() == 3, "q must be (n_heads, q_len_flatten, d_head)");
   TORCH_CHECK(k_pool.dim() == 4 && v_pool.dim() == 4, "pools must be (num_blocks, n_kv_heads, block_size, d_head)");
   TORCH_CHECK(q.size(-1) == k_pool.size(-1) && q.size(-1) == v_pool.size(-1), "d_head mismatch");
@@ -63,7 +70,8 @@ void check_pools(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor
 }  // namespace
 
 torch::Tensor PagedAttentionGemvCuda(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
-                                     torch::Tensor kv_page_tables, torch::Tensor kv_lens, int64_t max_kv_len) {
+                                     torch::Tensor kv_page_tables, torch::Tensor kv_lens, int64_t max_kv_len,
+                                     bool out_token_major) {
   check_pools(q, k_pool, v_pool);
   TORCH_CHECK(kv_page_tables.scalar_type() == torch::kInt32 && kv_lens.scalar_type() == torch::kInt32,
               "kv_page_tables and kv_lens must be int32");
@@ -76,13 +84,14 @@ torch::Tensor PagedAttentionGemvCuda(torch::Tensor q, torch::Tensor k_pool, torc
   TORCH_CHECK(kv_page_tables.size(0) == num_seqs && kv_lens.numel() == num_seqs,
               "one block table row and one kv_len per sequence");
   c10::cuda::CUDAGuard guard(q.device());
-  auto out = torch::empty_like(q);
+  auto out = new_out(q, out_token_major);
   const size_t ws_bytes = fvb_paged_attention_decode_workspace_size(num_seqs, n_heads, int(k_pool.size(1)), head_dim,
                                                                     int(max_kv_len));
   torch::Tensor ws;
   if (ws_bytes > 0) ws = torch::empty({int64_t(ws_bytes)}, q.options().dtype(torch::kUInt8));
-  check_status(fvb_paged_attention_decode(q.data_ptr(), out.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
-                                          k_pool.size(0), n_heads, int(k_pool.size(1)), head_dim,
+  check_status(fvb_paged_attention_decode_strided(q.data_ptr(), q.stride(1), q.stride(0), out.data_ptr(),
+                                                  out.stride(1), out.stride(0), k_pool.data_ptr(), v_pool.data_ptr(),
+                                                  k_pool.size(0), n_heads, int(k_pool.size(1)), head_dim,
                                           int(k_pool.size(2)), num_seqs, kv_page_tables.data_ptr<int32_t>(),
                                           int(kv_page_tables.size(1)), kv_lens.data_ptr<int32_t>(), int(max_kv_len),
                                           dtype_code(q.scalar_type()), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes,
@@ -93,7 +102,7 @@ torch::Tensor PagedAttentionGemvCuda(torch::Tensor q, torch::Tensor k_pool, torc
 
 torch::Tensor PagedAttentionGemmCuda(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                                      torch::Tensor cu_seqlens, int64_t max_q_len, torch::Tensor kv_page_tables,
-                                     torch::Tensor kv_lens, torch::Tensor positions) {
+                                     torch::Tensor kv_lens, torch::Tensor positions, bool out_token_major) {
   check_pools(q, k_pool, v_pool);
   for (const auto* t : {&cu_seqlens, &kv_page_tables, &kv_lens, &positions}) {
     TORCH_CHECK(t->scalar_type() == torch::kInt32, "metadata tensors must be int32");
@@ -108,13 +117,15 @@ torch::Tensor PagedAttentionGemmCuda(torch::Tensor q, torch::Tensor k_pool, torc
   const int head_dim = int(q.size(2));
   TORCH_CHECK(positions.numel() == q_len_flatten, "one position per query token");
   c10::cuda::CUDAGuard guard(q.device());
-  auto out = torch::empty({n_heads, q_len_flatten, head_dim}, q.options());
+  auto out = new_out(q, out_token_major);
   const size_t ws_bytes = fvb_paged_attention_prefill_workspace_size(num_seqs, n_heads, int(k_pool.size(1)), head_dim,
                                                                      q_len_flatten, int(max_q_len));
   torch::Tensor ws;
   if (ws_bytes > 0) ws = torch::empty({int64_t(ws_bytes)}, q.options().dtype(torch::kUInt8));
-  check_status(fvb_paged_attention_prefill(q.data_ptr(), out.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
-                                           k_pool.size(0), n_heads, int(k_pool.size(1)), head_dim,
+  check_status(fvb_paged_attention_prefill_strided(q.data_ptr(), q.stride(1), q.stride(0), out.data_ptr(),
+                                                   out.stride(1), out.stride(0), k_pool.data_ptr(),
+                                                   v_pool.data_ptr(), k_pool.size(0), n_heads, int(k_pool.size(1)),
+                                                   head_dim,
                                            int(k_pool.size(2)), num_seqs, q_len_flatten,
                                            cu_seqlens.data_ptr<int32_t>(), int(max_q_len),
                                            kv_page_tables.data_ptr<int32_t>(), int(kv_page_tables.size(1)),
@@ -147,6 +158,35 @@ void StoreKVCacheCuda(torch::Tensor k, torch::Tensor v, torch::Tensor k_pool, to
                                  int(k.size(1)), int(k.size(2)), int(k_pool.size(2)), dtype_code(k.scalar_type()),
                                  stream_of(k)),
                "StoreKVCacheCuda");
+}
+
+// positions, cu_seqlens, kv_lens, -1-padded block tables and slot mapping from
+// per-sequence counts and a flat block list (cu_blocks: exclusive scan of the row lengths).
+std::vector<torch::Tensor> BuildVarlenMetadataCuda(torch::Tensor num_computed, torch::Tensor num_new,
+                                                   torch::Tensor flat_blocks, torch::Tensor cu_blocks,
+                                                   int64_t max_blocks_per_seq, int64_t num_tokens) {
+  for (const auto* t : {&num_computed, &num_new, &flat_blocks, &cu_blocks}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32 && t->is_contiguous(),
+                "num_computed, num_new, flat_blocks and cu_blocks must be contiguous int32 CUDA tensors");
+  }
+  const int64_t B = num_computed.numel();
+  TORCH_CHECK(B > 0 && num_new.numel() == B && cu_blocks.numel() == B + 1, "one count per sequence, B + 1 cu_blocks");
+  c10::cuda::CUDAGuard guard(num_computed.device());
+  auto opt = num_computed.options();
+  auto positions = torch::empty({num_tokens}, opt);
+  auto cu_seqlens = torch::empty({B + 1}, opt);
+  auto kv_lens = torch::empty({B}, opt);
+  auto tables = torch::empty({B, max_blocks_per_seq}, opt);
+  auto slots = torch::empty({num_tokens}, opt.dtype(torch::kInt64));
+  check_status(fvb_build_varlen_metadata(num_computed.data_ptr<int32_t>(), num_new.data_ptr<int32_t>(), int(B),
+                                         flat_blocks.numel() ? flat_blocks.data_ptr<int32_t>() : nullptr,
+                                         flat_blocks.numel(), cu_blocks.data_ptr<int32_t>(), int(max_blocks_per_seq),
+                                         num_tokens, num_tokens ? positions.data_ptr<int32_t>() : nullptr,
+                                         cu_seqlens.data_ptr<int32_t>(), kv_lens.data_ptr<int32_t>(),
+                                         max_blocks_per_seq ? tables.data_ptr<int32_t>() : nullptr,
+                                         num_tokens ? slots.data_ptr<int64_t>() : nullptr, stream_of(num_computed)),
+               "BuildVarlenMetadataCuda");
+  return {positions, cu_seqlens, kv_lens, tables, slots};
 }
 
 // Fused q/k RMSNorm + rotary embedding + KV write; returns q in the head-major
@@ -228,11 +268,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("kMaxKVLenNonSplit") = fvb_max_kv_len();
   m.attr("kKVLenPerPage") = fvb_kv_len_per_page();
   m.attr("kDimHead") = fvb_dim_head();
-  m.def("PagedAttentionGemvCuda", &PagedAttentionGemvCuda, "decode paged attention (split-KV, sm_100a)");
-  m.def("PagedAttentionGemmCuda", &PagedAttentionGemmCuda, "varlen chunked-prefill paged attention (sm_100a)");
+  m.def("PagedAttentionGemvCuda", &PagedAttentionGemvCuda, "decode paged attention (split-KV, sm_100a)",
+        py::arg("q"), py::arg("k_pool"), py::arg("v_pool"), py::arg("kv_page_tables"), py::arg("kv_lens"),
+        py::arg("max_kv_len"), py::arg("out_token_major") = false);
+  m.def("PagedAttentionGemmCuda", &PagedAttentionGemmCuda, "varlen chunked-prefill paged attention (sm_100a)",
+        py::arg("q"), py::arg("k_pool"), py::arg("v_pool"), py::arg("cu_seqlens"), py::arg("max_q_len"),
+        py::arg("kv_page_tables"), py::arg("kv_lens"), py::arg("positions"), py::arg("out_token_major") = false);
   m.def("StoreKVCacheCuda", &StoreKVCacheCuda, "slot-mapped KV-cache write");
   m.def("BuildSlotMappingCuda", &BuildSlotMappingCuda, "slot of every new token from positions and block tables",
         py::arg("positions"), py::arg("cu_seqlens") = py::none(), py::arg("block_tables"));
+  m.def("BuildVarlenMetadataCuda", &BuildVarlenMetadataCuda,
+        "positions, cu_seqlens, kv_lens, padded block tables and slot mapping from per-sequence counts");
   m.def("QKNormRopeStoreCuda", &QKNormRopeStoreCuda,
         "fused q/k RMSNorm + rotary embedding + KV-cache write; returns q as (n_heads, num_tokens, d_head)");
   m.def("ReadDeviceError", &ReadDeviceError, "read and clear the device error word (synchronizes)");
@@ -241,16 +287,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 TORCH_LIBRARY(femtovllm_b200, m) {
   m.def(
       "paged_attention_decode(Tensor q, Tensor k_pool, Tensor v_pool, Tensor block_tables, Tensor kv_lens, "
-      "int max_kv_len) -> Tensor");
+      "int max_kv_len, bool out_token_major=False) -> Tensor");
   m.def(
       "paged_attention_prefill(Tensor q, Tensor k_pool, Tensor v_pool, Tensor cu_seqlens, int max_q_len, "
-      "Tensor block_tables, Tensor kv_lens, Tensor positions) -> Tensor");
+      "Tensor block_tables, Tensor kv_lens, Tensor positions, bool out_token_major=False) -> Tensor");
   m.def("store_kvcache(Tensor k, Tensor v, Tensor(a!) k_pool, Tensor(b!) v_pool, Tensor slot_mapping) -> ()");
   m.def("build_slot_mapping(Tensor positions, Tensor? cu_seqlens, Tensor block_tables) -> Tensor");
   m.def(
       "qk_norm_rope_store(Tensor q, Tensor k, Tensor v, Tensor q_norm_weight, Tensor k_norm_weight, float eps, "
       "Tensor rope_cos, Tensor rope_sin, Tensor positions, Tensor(a!) k_pool, Tensor(b!) v_pool, "
       "Tensor slot_mapping) -> Tensor");
+  m.def(
+      "build_varlen_metadata(Tensor num_computed, Tensor num_new, Tensor flat_blocks, Tensor cu_blocks, "
+      "int max_blocks_per_seq, int num_tokens) -> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
@@ -259,4 +308,5 @@ TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
   m.impl("store_kvcache", &StoreKVCacheCuda);
   m.impl("build_slot_mapping", &BuildSlotMappingCuda);
   m.impl("qk_norm_rope_store", &QKNormRopeStoreCuda);
+  m.impl("build_varlen_metadata", &BuildVarlenMetadataCuda);
 }

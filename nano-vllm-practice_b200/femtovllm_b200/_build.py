@@ -52,6 +52,7 @@ CU_SOURCES = [
     "capi.cu",
     "store_kvcache.cu",
     "qk_norm_rope.cu",
+    "metadata.cu",
     "decode.cu",
     "decode_noalloc.cu",
     "prefill_simt.cu",

@@ -48,6 +48,11 @@ _SIGNATURES = {
     "fvb_build_slot_mapping": (
         c_int, [c_void_p, c_int64, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]
     ),
+    "fvb_build_varlen_metadata": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p],
+    ),
     "fvb_qk_norm_rope_store": (
         c_int,
         [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
@@ -59,6 +64,17 @@ _SIGNATURES = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int,
          c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    ),
+    "fvb_paged_attention_decode_strided": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
+         c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    ),
+    "fvb_paged_attention_prefill_strided": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
+         c_int, c_int, c_int64, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_size_t,
+         c_void_p],
     ),
     "fvb_paged_attention_prefill_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int64, c_int]),
     "fvb_paged_attention_prefill": (

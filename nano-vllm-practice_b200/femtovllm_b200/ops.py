@@ -51,6 +51,20 @@ def _ensure_valid_tensor(t: torch.Tensor, name: str) -> torch.Tensor:
     return t
 
 
+def _q_view(q: torch.Tensor) -> torch.Tensor:
+    """q as the kernels can read it in place: any ``(n_heads, T, d_head)`` view whose
+    ``d_head`` is contiguous and whose token / head strides are 16-byte multiples (for
+    example ``q_thd.transpose(0, 1)`` of the projection output); anything else is copied,
+    as the reference's ``_ensure_valid_tensor`` does (``ops/__init__.py:29-44``)."""
+    if not q.is_cuda:
+        raise ValueError(f"Argument 'q' must be a CUDA tensor. Got device={q.device}")
+    es = q.element_size()
+    if q.dim() == 3 and q.stride(2) == 1 and (q.stride(0) * es) % 16 == 0 and (q.stride(1) * es) % 16 == 0 \
+            and q.data_ptr() % 16 == 0:
+        return q
+    return q.contiguous()
+
+
 def paged_attention_gemv(
     q: torch.Tensor,
     k_pool: torch.Tensor,
@@ -59,13 +73,20 @@ def paged_attention_gemv(
     kv_lens: torch.Tensor,
     max_kv_len: int,
     impl=None,
+    out_token_major: bool = False,
 ) -> torch.Tensor:
-    """Decode paged attention; returns ``(n_heads, B, d_head)`` in q's dtype."""
-    q = _ensure_valid_tensor(q, "q")
+    """Decode paged attention; returns ``(n_heads, B, d_head)`` in q's dtype.
+
+    ``out_token_major=True`` returns the same shape as a view of a ``(B, n_heads, d_head)``
+    buffer, so ``out.transpose(0, 1).reshape(B, n_heads * d_head)`` (the o_proj input,
+    ``qwen3.py:278``) is free.  ``q`` may be a transposed view (see ``_q_view``).
+    """
+    q = _q_view(q)
     for t, n in ((k_pool, "k_pool"), (v_pool, "v_pool"), (kv_page_tables, "kv_page_tables"), (kv_lens, "kv_lens")):
         if not t.is_cuda:
             raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
-    return _cuda_backend.PagedAttentionGemvCuda(q, k_pool, v_pool, kv_page_tables, kv_lens, int(max_kv_len))
+    return _cuda_backend.PagedAttentionGemvCuda(q, k_pool, v_pool, kv_page_tables, kv_lens, int(max_kv_len),
+                                                bool(out_token_major))
 
 
 def paged_attention_gemm(
@@ -81,14 +102,16 @@ def paged_attention_gemm(
     kv_lens: torch.Tensor,
     positions: torch.Tensor,
     impl=None,
+    out_token_major: bool = False,
 ) -> torch.Tensor:
     """Varlen chunked-prefill attention; returns ``(n_heads, q_len_flatten, d_head)``.
 
     ``Q_TILE_SIZE``, ``cu_q_tiles`` and ``q_tile_to_seq_idx`` are the
     reference Triton kernel's tiling metadata (``model_runner.py:174-202``);
     they are accepted and unused, since the kernel tiles the queries itself.
+    ``out_token_major`` and strided ``q`` as for ``paged_attention_gemv``.
     """
-    q = _ensure_valid_tensor(q, "q")
+    q = _q_view(q)
     for t, n in (
         (k_pool, "k_pool"),
         (v_pool, "v_pool"),
@@ -100,7 +123,7 @@ def paged_attention_gemm(
         if not t.is_cuda:
             raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
     return _cuda_backend.PagedAttentionGemmCuda(
-        q, k_pool, v_pool, cu_seqlens, int(max_q_len), kv_page_tables, kv_lens, positions
+        q, k_pool, v_pool, cu_seqlens, int(max_q_len), kv_page_tables, kv_lens, positions, bool(out_token_major)
     )
 
 
@@ -140,6 +163,35 @@ def build_slot_mapping(
         if not t.is_cuda:
             raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
     return _cuda_backend.BuildSlotMappingCuda(positions.contiguous(), cu_seqlens, block_tables.contiguous())
+
+
+def build_varlen_metadata(
+    num_computed: torch.Tensor,
+    num_new: torch.Tensor,
+    flat_blocks: torch.Tensor,
+    cu_blocks: torch.Tensor,
+    max_blocks_per_seq: int,
+    num_tokens: int,
+) -> dict:
+    """Attention metadata of one step from per-sequence counts, built on the device.
+
+    For sequence ``s`` with ``num_computed[s]`` cached and ``num_new[s]`` new tokens
+    (decode: 1), as ``ModelRunner._route_prefill`` / ``_route_decode`` build them on the
+    host (``model_runner.py:186-205, 280-290``) and ``pad_block_tables`` (``:46-72``):
+    ``positions`` (``range(p, p + n)`` per sequence), ``cu_seqlens``, ``kv_lens = p + n``,
+    ``block_tables`` (``-1``-padded to ``max_blocks_per_seq``) and ``slot_mapping``.
+    ``flat_blocks`` holds every sequence's blocks back to back, ``cu_blocks`` (``B + 1``)
+    where each row starts; ``num_tokens`` is ``sum(num_new)`` (the scheduler knows it).
+    """
+    for t, n in ((num_computed, "num_computed"), (num_new, "num_new"), (flat_blocks, "flat_blocks"),
+                 (cu_blocks, "cu_blocks")):
+        if not t.is_cuda:
+            raise ValueError(f"Argument '{n}' must be a CUDA tensor. Got device={t.device}")
+    i32 = lambda t: t.to(torch.int32).contiguous()  # noqa: E731
+    pos, cu, kv, tables, slots = _cuda_backend.BuildVarlenMetadataCuda(
+        i32(num_computed), i32(num_new), i32(flat_blocks), i32(cu_blocks), int(max_blocks_per_seq), int(num_tokens)
+    )
+    return {"positions": pos, "cu_seqlens": cu, "kv_lens": kv, "block_tables": tables, "slot_mapping": slots}
 
 
 def qk_norm_rope_store(

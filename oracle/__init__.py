@@ -9,7 +9,9 @@ parts of the attention hot path:
 * decode paged attention over ``block_tables`` with GQA,
 * varlen chunked-prefill causal attention over prefix-cached paged KV,
 * the stage before them: q/k RMSNorm, rotary embedding and the KV write
-  (``oracle/qk_norm_rope.py``).
+  (``oracle/qk_norm_rope.py``),
+* the per-step metadata (positions, cu_seqlens, kv_lens, padded block tables)
+  the engine builds for them (``oracle/metadata.py``).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 ``--impl reference`` legs of ``bench.py`` may import it, and only as the
@@ -40,3 +42,4 @@ from oracle.qk_norm_rope import (  # noqa: F401
     rms_norm,
     rope_tables,
 )
+from oracle.metadata import varlen_metadata  # noqa: F401,E402

@@ -46,7 +46,7 @@ def golden_after(d: dict, which: str) -> np.ndarray:
     return pool
 
 
-GOLDEN_CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("norm_rope_"))
+GOLDEN_CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("norm_rope_", "metadata_")))
 NORM_ROPE_CASES = sorted(p.stem for p in GOLDEN.glob("norm_rope_*.npz"))
 
 

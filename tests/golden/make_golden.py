@@ -27,6 +27,10 @@ The ``norm_rope_*`` fixtures instead keep the reference's q_norm / k_norm
 pool rows their write loops produce: the stage that ``qk_norm_rope_store``
 fuses.
 
+``metadata_routes.npz`` records the VarlenAttnMetadata that the reference's own
+``ModelRunner._route_prefill`` / ``_route_decode`` (``model_runner.py:159-339``)
+build from scheduled sequences, for ``build_varlen_metadata``.
+
 All inputs are bf16-representable (stored as bf16 bits) so one fixture serves
 both the fp32 and the bf16 checks; the reference runs in fp32.  Each fixture
 stores the pools before the write and only the rows the reference changed.
@@ -320,6 +324,58 @@ def run_reference_norm_rope(case, femtovllm, QwenSelfAttention, VarlenAttnMetada
     }
 
 
+def run_reference_routes(ref: Path):
+    """Per-step metadata as the reference's ModelRunner builds it (model_runner.py:159-339): its own
+    _route_prefill / _route_decode run on a stand-in object whose model records the
+    VarlenAttnMetadata it is handed."""
+    from femtovllm.engine.model_runner import ModelRunner
+
+    seen = {}
+
+    class _Model:
+        def forward_varlen(self, idx_flatten, varlen_attn_metadata, skip_lm_head=True):
+            seen["md"] = varlen_attn_metadata
+            return None
+
+    runner = types.SimpleNamespace(device="cpu", model=_Model())
+    runner.pad_block_tables = lambda t: ModelRunner.pad_block_tables(runner, t)
+    rng = np.random.default_rng(41)
+    out = {}
+    # Prefill route: new chunks over cached prefixes (0, page edges, long), ragged table rows.
+    num_computed = np.array([0, 15, 16, 100, 2047, 0, 31], np.int64)
+    num_new = np.array([5, 1, 33, 64, 1, 300, 17], np.int64)
+    # Decode route: one new token per sequence.
+    dec_computed = np.array([0, 15, 16, 17, 1000, 4095], np.int64)
+    for route, (pc, pn) in {"prefill": (num_computed, num_new), "decode": (dec_computed, np.ones(6, np.int64))}.items():
+        free = [int(b) for b in rng.permutation(4096)]
+        tables = []
+        for p, n in zip(pc, pn):
+            need = (int(p + n) + PAGE - 1) // PAGE + int(rng.integers(0, 3))  # rows may run past kv_len
+            tables.append([free.pop() for _ in range(need)])
+        scheduled = [(types.SimpleNamespace(num_computed_tokens=int(p), token_ids=list(range(int(p + n)))), int(n))
+                     for p, n in zip(pc, pn)]
+        if route == "prefill":
+            ModelRunner._route_prefill(runner, scheduled, None, None, tables)
+        else:
+            ModelRunner._route_decode(runner, scheduled, None, None, tables)
+        md = seen["md"]
+        flat = np.asarray([b for t in tables for b in t], np.int32)
+        cu_blocks = np.concatenate([[0], np.cumsum([len(t) for t in tables])]).astype(np.int32)
+        out[f"{route}_num_computed"] = pc.astype(np.int32)
+        out[f"{route}_num_new"] = pn.astype(np.int32)
+        out[f"{route}_flat_blocks"] = flat
+        out[f"{route}_cu_blocks"] = cu_blocks
+        out[f"{route}_positions"] = md.positions.numpy()
+        out[f"{route}_kv_lens"] = md.kv_lens.numpy()
+        out[f"{route}_block_tables"] = md.block_tables.numpy()
+        out[f"{route}_max_q_len"] = np.int32(md.max_q_len)
+        out[f"{route}_max_kv_len"] = np.int32(md.max_kv_len)
+        if md.cu_seqlens is not None:
+            out[f"{route}_cu_seqlens"] = md.cu_seqlens.numpy()
+    np.savez_compressed(HERE / "metadata_routes.npz", **out)
+    print("metadata_routes: prefill T=%d, decode B=%d" % (int(num_new.sum()), len(dec_computed)))
+
+
 def _bits(t: torch.Tensor) -> np.ndarray:
     return t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
 
@@ -333,9 +389,13 @@ def _changed_rows(before, after):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--which", choices=["attention", "norm_rope", "all"], default="all")
+    ap.add_argument("--which", choices=["attention", "norm_rope", "metadata", "all"], default="all")
     args = ap.parse_args()
     femtovllm, QSA, VAM = _import_reference(args.reference)
+    if args.which in ("metadata", "all"):
+        run_reference_routes(args.reference)
+        if args.which == "metadata":
+            return
     if args.which in ("norm_rope", "all"):
         for case in norm_rope_cases():
             r = run_reference_norm_rope(case, femtovllm, QSA, VAM)

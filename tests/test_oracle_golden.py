@@ -120,3 +120,24 @@ def test_norm_rope_oracle_catches_a_planted_rotation_error():
     s = d["sin_rows"][:, None, :].astype(np.float64)
     bad = c * x + s * np.concatenate([x[..., half:], -x[..., :half]], axis=-1)
     assert np.abs(bad.transpose(1, 0, 2) - d["q_ref"]).max() > 1e-2
+
+
+# ---------------------------------------------------------------------------
+# per-step metadata (metadata_routes.npz, from the reference's ModelRunner routes)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("route", ["prefill", "decode"])
+def test_varlen_metadata_matches_reference_routes(route):
+    from conftest import GOLDEN
+
+    z = np.load(GOLDEN / "metadata_routes.npz")
+    flat, cu_b = z[f"{route}_flat_blocks"], z[f"{route}_cu_blocks"]
+    tables = [flat[cu_b[i] : cu_b[i + 1]].tolist() for i in range(len(cu_b) - 1)]
+    md = oracle.varlen_metadata(z[f"{route}_num_computed"], z[f"{route}_num_new"], tables)
+    assert np.array_equal(md["positions"], z[f"{route}_positions"])
+    assert np.array_equal(md["kv_lens"], z[f"{route}_kv_lens"])
+    assert np.array_equal(md["block_tables"], z[f"{route}_block_tables"])
+    assert md["max_q_len"] == int(z[f"{route}_max_q_len"]) and md["max_kv_len"] == int(z[f"{route}_max_kv_len"])
+    if f"{route}_cu_seqlens" in z.files:
+        assert np.array_equal(md["cu_seqlens"], z[f"{route}_cu_seqlens"])
