@@ -53,8 +53,8 @@ struct DecodeTraits {
   static constexpr int kSlots = kConsumerWarps;
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kSlots * kStageBytes;
-  static constexpr int kOffQ = 2 * kSlots * kStageBytes;      // float [NREP][D], pre-scaled to log2 units
-  static constexpr int kOffP = kOffQ + NREP * D * 4;          // float [warp][token][NREP]
+  static constexpr int kOffQ = 2 * kSlots * kStageBytes;      // T [NREP][D], as given (scaled after the dot)
+  static constexpr int kOffP = kOffQ + NREP * D * kEsize;     // float [warp][token][NREP]
   static constexpr int kOffBar = kOffP + kConsumerWarps * kStageTokens * NREP * 4;
   static constexpr int kSmemBytes = kOffBar + 2 * kSlots * 8 + 1024;  // + 1024-B alignment slack
   // Warp-merge scratch (float acc[warp][NREP][D], m[warp][NREP], l[warp][NREP]) aliases the ring.
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
   using Tr = DecodeTraits<T, D, NREP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* qs = reinterpret_cast<float*>(smem + Tr::kOffQ);
+  T* qs = reinterpret_cast<T*>(smem + Tr::kOffQ);
   float* ps = reinterpret_cast<float*>(smem + Tr::kOffP);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Tr::kOffBar);
   uint64_t* empty = full + Tr::kSlots;
@@ -152,14 +152,13 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     }
     fence_mbar_init();
   }
-  // q for the NREP heads of this group, fp32, scaled so scores are in log2 units.
-  {
-    const float scale = kLog2e * rsqrtf(float(D));
-    for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
-      const int r = e / D, d = e % D;
-      qs[e] = Elem<T>::to_f(q[int64_t(b) * lay.q_ts + int64_t(kvh * NREP + r) * lay.q_hs + d]) * scale;
-    }
+  // q for the NREP heads of this group, in its own type: 16-byte reads then cover
+  // 8 (16-bit) dims; the log2-domain scale is applied to the finished dot product.
+  for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
+    const int r = e / D, d = e % D;
+    qs[e] = q[int64_t(b) * lay.q_ts + int64_t(kvh * NREP + r) * lay.q_hs + d];
   }
+  const float qk_scale = kLog2e * rsqrtf(float(D));
   __syncthreads();
 
   const int32_t* table = block_tables + int64_t(b) * max_blocks_per_seq;
@@ -237,18 +236,20 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
       unpack16<T>(lds_v4(kaddr), kf);
 #pragma unroll
       for (int r = 0; r < NREP; ++r) {
+        float qf[Tr::kVec];  // one broadcast 16-byte read per head and chunk
+        unpack16<T>(lds_v4(qs_addr + (r * D + c * Tr::kVec) * Tr::kEsize), qf);
 #pragma unroll
         for (int e = 0; e < Tr::kVec; e += 4) {
-          const float4 qv = *reinterpret_cast<const float4*>(qs + r * D + c * Tr::kVec + e);
-          sp[r][0] = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(kf[e + 0], kf[e + 1]), sp[r][0]);
-          sp[r][1] = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(kf[e + 2], kf[e + 3]), sp[r][1]);
+          sp[r][0] = __ffma2_rn(make_float2(qf[e + 0], qf[e + 1]), make_float2(kf[e + 0], kf[e + 1]), sp[r][0]);
+          sp[r][1] = __ffma2_rn(make_float2(qf[e + 2], qf[e + 3]), make_float2(kf[e + 2], kf[e + 3]), sp[r][1]);
         }
       }
     }
     float s[NREP];
 #pragma unroll
-    for (int r = 0; r < NREP; ++r) s[r] = (sp[r][0].x + sp[r][1].x) + (sp[r][0].y + sp[r][1].y);
+    for (int r = 0; r < NREP; ++r) s[r] = ((sp[r][0].x + sp[r][1].x) + (sp[r][0].y + sp[r][1].y)) * qk_scale;
     const bool valid = lane < nvalid;
+    float pv_[NREP];
 #pragma unroll
     for (int r = 0; r < NREP; ++r) {
       const float sr = valid ? s[r] : -INFINITY;
@@ -259,7 +260,18 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
       l[r] = l[r] * corr + p;
 #pragma unroll
       for (int i = 0; i < Tr::kDPL; ++i) acc[r][i] *= corr;
-      pw[lane * NREP + r] = p;
+      pv_[r] = p;
+    }
+    // this lane's NREP probabilities in one store (the [token][NREP] layout the PV loop reads)
+    if constexpr (NREP % 4 == 0) {
+#pragma unroll
+      for (int r = 0; r < NREP; r += 4)
+        *reinterpret_cast<float4*>(pw + lane * NREP + r) = make_float4(pv_[r], pv_[r + 1], pv_[r + 2], pv_[r + 3]);
+    } else if constexpr (NREP == 2) {
+      *reinterpret_cast<float2*>(pw + lane * NREP) = make_float2(pv_[0], pv_[1]);
+    } else {
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) pw[lane * NREP + r] = pv_[r];
     }
     __syncwarp();
     // acc[r][:] += sum_t p[t][r] * V[t][lane dims]
