@@ -80,6 +80,13 @@ int check_attention(const void* q, const void* out, const void* k_pool, const vo
   return FVB_OK;
 }
 
+// Decode route: 16-bit GQA >= 8 runs on the tcgen05 attention kernel (measured 1.68x
+// the SIMT split-KV kernel at GQA 8, config-2 lengths); smaller groups and fp32 keep
+// the split-KV kernel, which is HBM-bound for them.
+bool decode_on_tensor_cores(int n_heads, int n_kv_heads, int dtype) {
+  return dtype != FVB_DTYPE_F32 && n_kv_heads > 0 && n_heads / n_kv_heads >= 8;
+}
+
 // q / out strides (elements): non-negative, and every row start 16-byte aligned
 // (the tensor-core prefill loads q rows with TMA and stores out rows as 16-byte vectors).
 int check_layout(const QOLayout& lay, int dtype) {
@@ -302,7 +309,12 @@ int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const i
 size_t fvb_paged_attention_decode_workspace_size(int num_seqs, int n_heads, int n_kv_heads, int head_dim,
                                                  int max_kv_len) {
   if (num_seqs <= 0 || !gqa_ok(n_heads, n_kv_heads)) return 0;
-  return plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count()).ws_bytes;
+  const size_t split_ws = plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count()).ws_bytes;
+  if (!decode_on_tensor_cores(n_heads, n_kv_heads, FVB_DTYPE_BF16)) return split_ws;
+  // 16-bit GQA >= 8 decodes on the tensor-core path (whose plan does not depend on the
+  // dtype); fp32 keeps the split-KV plan.  The size covers both.
+  const size_t tc_ws = plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, num_seqs, 1, FVB_DTYPE_BF16).ws_bytes;
+  return split_ws > tc_ws ? split_ws : tc_ws;
 }
 
 int fvb_paged_attention_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
@@ -330,6 +342,19 @@ int fvb_paged_attention_decode_strided(const void* q, int64_t q_token_stride, in
   if (st) return st;
   if (num_seqs == 0) return FVB_OK;
   if (max_kv_len < 0 || int64_t(max_kv_len) > int64_t(max_blocks_per_seq) * kPageSize) return FVB_ERR_INVALID_ARGUMENT;
+  if (decode_on_tensor_cores(n_heads, n_kv_heads, dtype)) {
+    // One 128-row tile per (sequence, kv head) holds the group's n_rep heads: the
+    // tcgen05 attention kernel in decode mode (no cu_seqlens / positions).
+    const PrefillPlan pp = plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, num_seqs, 1, dtype);
+    if (!workspace || workspace_bytes < pp.ws_bytes) return FVB_ERR_WORKSPACE_TOO_SMALL;
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return FVB_ERR_MISALIGNED;
+    cudaError_t e;
+    int* err = device_error_ptr(&e);
+    if (!err) return cuda_status(e);
+    return cuda_status(launch_prefill(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
+                                      num_seqs, nullptr, 1, block_tables, max_blocks_per_seq, kv_lens, nullptr, dtype,
+                                      pp, lay, workspace, err, static_cast<cudaStream_t>(stream)));
+  }
   const DecodePlan plan = plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count());
   if (plan.ws_bytes > 0 && (!workspace || workspace_bytes < plan.ws_bytes)) return FVB_ERR_WORKSPACE_TOO_SMALL;
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255)) return FVB_ERR_MISALIGNED;

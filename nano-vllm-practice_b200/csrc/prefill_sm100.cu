@@ -7,6 +7,10 @@
 // PagedAttentionGemmKernel (csrc/paged_attention/paged_attention_gemm.cu:24-302).
 // Semantics (the reference's): key j is visible to query i of sequence s iff
 // j < kv_lens[s] and j <= positions[i]; softmax in fp32; output cast to T.
+// Decode mode (cu_seqlens == positions == nullptr): token s is sequence s's one
+// query at position kv_lens[s] - 1; the decode entry points use it for GQA >= 8,
+// where the n_rep heads of a group fill a 128-row tile well enough that the
+// tensor cores beat the SIMT split-KV decode.
 //
 // Query tile = 128 rows: 128 / n_rep consecutive query tokens of one sequence
 // x the n_rep query heads of one kv head's GQA group, so every K/V byte
@@ -141,7 +145,8 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __res
     int v = 0;
     if (p < num_seqs) {
       const int s = order[p];
-      const int ql = __ldg(cu_seqlens + s + 1) - __ldg(cu_seqlens + s);
+      // decode mode (cu_seqlens == nullptr): one query token per sequence
+      const int ql = cu_seqlens ? __ldg(cu_seqlens + s + 1) - __ldg(cu_seqlens + s) : 1;
       const int tiles = ql > 0 ? (ql + tile_tokens - 1) / tile_tokens : 0;
       v = (tiles + 1) / 2;
     }
@@ -204,7 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     if (__ldg(cu_items + mid) <= item) lo = mid; else hi = mid - 1;
   }
   const int s = __ldg(order + lo);
-  const int q_begin = __ldg(cu_seqlens + s), q_end = __ldg(cu_seqlens + s + 1);
+  // decode mode (cu_seqlens == nullptr): token s of sequence s, at position kv_len - 1
+  const int q_begin = cu_seqlens ? __ldg(cu_seqlens + s) : s;
+  const int q_end = cu_seqlens ? __ldg(cu_seqlens + s + 1) : s + 1;
   const int ntq = (q_end - q_begin + TOK - 1) / TOK;
   const int pair = (ntq + 1) / 2 - 1 - (item - __ldg(cu_items + lo));  // last (longest-context) pair first
   const bool has1 = 2 * pair + 1 < ntq;
@@ -219,7 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     t0[i] = q_begin + (2 * pair + i) * TOK;
     t_last[i] = min(t0[i] + TOK, q_end) - 1;
     const bool live = i == 0 || has1;
-    p_last[i] = (live && kv_len > 0) ? max(min(__ldg(positions + t_last[i]), kv_len - 1), 0) : -1;
+    const int p_tok = positions ? __ldg(positions + t_last[i]) : kv_len - 1;
+    p_last[i] = (live && kv_len > 0) ? max(min(p_tok, kv_len - 1), 0) : -1;
     nkv[i] = p_last[i] >= 0 ? p_last[i] / kTileN + 1 : 0;
   }
   const int n_kv = max(nkv[0], nkv[1]);
@@ -406,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     const int g = r / TOK, tok = t0[i] + r % TOK;
     const bool row_valid = tok <= t_last[i];
     const int head = kvh * NREP + g;
-    int pos = row_valid ? __ldg(positions + tok) : p_last[i];
+    int pos = (row_valid && positions) ? __ldg(positions + tok) : p_last[i];
     pos = max(min(pos, kv_len - 1), 0);
     const float scale = kLog2e * rsqrtf(float(D));
     const float2 scale2 = make_float2(scale, scale);
