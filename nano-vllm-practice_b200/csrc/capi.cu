@@ -58,10 +58,9 @@ int cuda_status(cudaError_t e) {
   return FVB_ERR_CUDA;
 }
 
+// Any whole GQA group (kv_head = q_head / (n_heads / n_kv_heads), as the reference).
 bool gqa_ok(int n_heads, int n_kv_heads) {
-  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads) return false;
-  const int r = n_heads / n_kv_heads;
-  return r == 1 || r == 2 || r == 4 || r == 8;
+  return n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0;
 }
 
 // Common checks of the attention entry points.
@@ -80,11 +79,11 @@ int check_attention(const void* q, const void* out, const void* k_pool, const vo
   return FVB_OK;
 }
 
-// Decode route: 16-bit GQA >= 8 runs on the tcgen05 attention kernel (measured 1.68x
-// the SIMT split-KV kernel at GQA 8, config-2 lengths); smaller groups and fp32 keep
-// the split-KV kernel, which is HBM-bound for them.
+// Decode route: 16-bit GQA >= 5 runs on the tcgen05 attention kernel (measured 1.68x
+// the SIMT split-KV kernel at GQA 8, config-2 lengths; groups of 5-7 pad to 8 heads on
+// either path); smaller groups and fp32 keep the split-KV kernel, HBM-bound for them.
 bool decode_on_tensor_cores(int n_heads, int n_kv_heads, int dtype) {
-  return dtype != FVB_DTYPE_F32 && n_kv_heads > 0 && n_heads / n_kv_heads >= 8;
+  return dtype != FVB_DTYPE_F32 && n_kv_heads > 0 && n_heads / n_kv_heads >= 5;
 }
 
 // q / out strides (elements): non-negative, and every row start 16-byte aligned

@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     const uint8_t* __restrict__ v_pool, int64_t num_blocks, int n_kv_heads, int num_seqs,
     const int32_t* __restrict__ block_tables, int max_blocks_per_seq, const int32_t* __restrict__ kv_lens,
     int kv_cap, int pages_per_split, int max_splits, float* __restrict__ ws_o, float* __restrict__ ws_lse,
-    const QOLayout lay, int* __restrict__ err) {
+    const QOLayout lay, int group, int chunks, int* __restrict__ err) {
   using Tr = DecodeTraits<T, D, NREP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -118,9 +118,14 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Tr::kOffBar);
   uint64_t* empty = full + Tr::kSlots;
 
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  // blockIdx.y = (kv head, chunk): a GQA group of `group` query heads is served in
+  // chunks of NREP heads; heads of the last chunk past the group are computed on a
+  // copy of a real head's q and never written.
+  const int split = blockIdx.x, kvh = blockIdx.y / chunks, chunk = blockIdx.y % chunks, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_heads = n_kv_heads * NREP;
+  const int n_heads = n_kv_heads * group;
+  const int head0 = kvh * group + chunk * NREP;       // query head of row r = head0 + r
+  const int nvh = min(NREP, group - chunk * NREP);    // rows that are real heads
   int kv_len = max(__ldg(kv_lens + b), 0);
   if (kv_len > kv_cap) {
     // Longer than max_kv_len or than the block table row: never read past either.
@@ -134,9 +139,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
   if (npages == 0) {
     // Empty context: the reference never produces one; emit zeros, not garbage.
     if (split == 0) {
-      for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
+      for (int e = threadIdx.x; e < nvh * D; e += blockDim.x) {
         const int r = e / D, d = e % D;
-        out[int64_t(b) * lay.o_ts + int64_t(kvh * NREP + r) * lay.o_hs + d] = Elem<T>::from_f(0.f);
+        out[int64_t(b) * lay.o_ts + int64_t(head0 + r) * lay.o_hs + d] = Elem<T>::from_f(0.f);
       }
     }
     return;
@@ -156,7 +161,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
   // 8 (16-bit) dims; the log2-domain scale is applied to the finished dot product.
   for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
     const int r = e / D, d = e % D;
-    qs[e] = q[int64_t(b) * lay.q_ts + int64_t(kvh * NREP + r) * lay.q_hs + d];
+    qs[e] = q[int64_t(b) * lay.q_ts + int64_t(head0 + min(r, nvh - 1)) * lay.q_hs + d];
   }
   const float qk_scale = kLog2e * rsqrtf(float(D));
   __syncthreads();
@@ -335,7 +340,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
       L += wl[w * NREP + r] * f;
       O += wacc[(w * NREP + r) * D + d] * f;
     }
-    const int head = kvh * NREP + r;
+    if (r >= nvh) continue;
+    const int head = head0 + r;
     if (nsplits == 1) {
       out[int64_t(b) * lay.o_ts + int64_t(head) * lay.o_hs + d] = Elem<T>::from_f(O / L);
     } else {
@@ -407,7 +413,7 @@ template <typename T, int D, int NREP>
 cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                             int n_kv_heads, int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
                             const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan, const QOLayout& lay,
-                            void* workspace, int* err, cudaStream_t stream) {
+                            int group, void* workspace, int* err, cudaStream_t stream) {
   using Tr = DecodeTraits<T, D, NREP>;
   const int kv_cap = int(std::min<int64_t>(std::min<int64_t>(max_kv_len, int64_t(max_blocks_per_seq) * kPageSize),
                                            int64_t(plan.max_splits) * plan.pages_per_split * kPageSize));
@@ -425,14 +431,15 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
   float* ws_lse = nullptr;
   if (plan.max_splits > 1) {
     ws_o = static_cast<float*>(workspace);
-    const size_t o_bytes = size_t(num_seqs) * n_kv_heads * NREP * plan.max_splits * D * 4;
+    const size_t o_bytes = size_t(num_seqs) * n_kv_heads * group * plan.max_splits * D * 4;
     ws_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((o_bytes + 255) & ~size_t(255)));
   }
-  dim3 grid(plan.max_splits, n_kv_heads, num_seqs);
+  const int chunks = (group + NREP - 1) / NREP;
+  dim3 grid(plan.max_splits, n_kv_heads * chunks, num_seqs);
   kern<<<grid, kDecodeThreads, Tr::kSmemBytes, stream>>>(
       kmap, static_cast<const T*>(q), static_cast<T*>(out), static_cast<const uint8_t*>(v_pool), num_blocks,
       n_kv_heads, num_seqs, block_tables, max_blocks_per_seq, kv_lens, kv_cap, plan.pages_per_split, plan.max_splits,
-      ws_o, ws_lse, lay, err);
+      ws_o, ws_lse, lay, group, chunks, err);
   ce = cudaGetLastError();
   if (ce != cudaSuccess || plan.max_splits <= 1) return ce;
   const size_t csmem = (size_t(plan.max_splits) + D / 32) * sizeof(float);
@@ -440,8 +447,8 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
     ce = cudaFuncSetAttribute(decode_combine_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(csmem));
     if (ce != cudaSuccess) return ce;
   }
-  decode_combine_kernel<T, D><<<unsigned(num_seqs * n_kv_heads * NREP), D, csmem, stream>>>(
-      ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap, num_seqs, n_kv_heads * NREP, plan.pages_per_split,
+  decode_combine_kernel<T, D><<<unsigned(num_seqs * n_kv_heads * group), D, csmem, stream>>>(
+      ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap, num_seqs, n_kv_heads * group, plan.pages_per_split,
       plan.max_splits, lay);
   return cudaGetLastError();
 }
@@ -451,22 +458,19 @@ cudaError_t dispatch_nrep(int nrep, const void* q, void* out, const void* k_pool
                           int64_t num_blocks, int n_kv_heads, int num_seqs, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan,
                           const QOLayout& lay, void* ws, int* err, cudaStream_t stream) {
-  switch (nrep) {
+#define FVB_DT_ARGS q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables, max_blocks_per_seq, \
+                    kv_lens, max_kv_len, plan, lay, nrep, ws, err, stream
+  switch (decode_tile_heads(nrep)) {
     case 1:
-      return launch_decode_t<T, D, 1>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
+      return launch_decode_t<T, D, 1>(FVB_DT_ARGS);
     case 2:
-      return launch_decode_t<T, D, 2>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
+      return launch_decode_t<T, D, 2>(FVB_DT_ARGS);
     case 4:
-      return launch_decode_t<T, D, 4>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
-    case 8:
-      return launch_decode_t<T, D, 8>(q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables,
-                                      max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, ws, err, stream);
+      return launch_decode_t<T, D, 4>(FVB_DT_ARGS);
     default:
-      return cudaErrorInvalidValue;
+      return launch_decode_t<T, D, 8>(FVB_DT_ARGS);
   }
+#undef FVB_DT_ARGS
 }
 
 }  // namespace
@@ -474,7 +478,9 @@ cudaError_t dispatch_nrep(int nrep, const void* q, void* out, const void* k_pool
 DecodePlan plan_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int max_kv_len, int num_sms) {
   DecodePlan p{};
   const int max_pages = std::max(1, (max_kv_len + kPageSize - 1) / kPageSize);
-  const int64_t units = int64_t(num_seqs) * n_kv_heads;
+  const int group = n_kv_heads > 0 ? n_heads / n_kv_heads : 1;
+  const int tile = decode_tile_heads(group);
+  const int64_t units = int64_t(num_seqs) * n_kv_heads * ((group + tile - 1) / tile);
   // Enough CTAs for ~4 waves of 3 resident CTAs per SM, but no split shorter
   // than 4 pages (64 tokens) and none longer than 64 pages (1024 tokens), so
   // the last wave's tail stays short for long contexts.

@@ -41,6 +41,10 @@ cudaError_t launch_build_slot_mapping(const int32_t* positions, int64_t num_toke
 
 // Split-KV plan of one decode launch.  Deterministic in its inputs and the
 // device's SM count, so the workspace size can be asked for ahead of the call.
+// Query heads one decode CTA serves: the GQA group size rounded up to 1, 2, 4 or 8.
+// Larger groups are served in chunks of 8 heads (K/V read once per chunk).
+inline int decode_tile_heads(int group) { return group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8; }
+
 struct DecodePlan {
   int pages_per_split;  // multiple of the 2-page stage
   int max_splits;       // ceil(ceil(max_kv_len / 16) / pages_per_split)

@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     const __grid_constant__ CUtensorMap vmap, T* __restrict__ out, int64_t q_len_flatten, int num_seqs,
     int n_kv_heads, int64_t num_blocks, const int32_t* __restrict__ cu_seqlens, const int32_t* __restrict__ order,
     const int32_t* __restrict__ cu_items, const int32_t* __restrict__ block_tables, int max_blocks_per_seq,
-    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, const QOLayout lay,
-    int* __restrict__ err) {
+    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, const QOLayout lay, int group,
+    int chunks, int* __restrict__ err) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;  // query tokens per tile
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -201,7 +201,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
 
   // ---- work item: (query-tile pair, kv head); the heaviest items have the lowest ids ----
-  const int item = int(blockIdx.x) / n_kv_heads, kvh = int(blockIdx.x) % n_kv_heads;
+  // CTA = (work item, kv head, chunk): a GQA group of `group` query heads is served in
+  // chunks of NREP heads (the tile's head slots); slots past the group load a real
+  // head's q and are never written.
+  const int units = n_kv_heads * chunks;
+  const int item = int(blockIdx.x) / units, unit = int(blockIdx.x) % units;
+  const int kvh = unit / chunks, chunk = unit % chunks;
+  const int head0 = kvh * group + chunk * NREP;     // query head of tile slot g = head0 + g
+  const int nvh = min(NREP, group - chunk * NREP);  // slots that are real heads
   if (item >= __ldg(cu_items + num_seqs)) return;
   int lo = 0, hi = num_seqs - 1;
   while (lo < hi) {
@@ -238,8 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   if (n_kv == 0) {  // empty context (never produced by the engine): zeros, not garbage
     for (int e = threadIdx.x; e < 2 * kTileM * D; e += kThreads) {
       const int i = e / (kTileM * D), r = (e / D) % kTileM, tok = t0[i] + r % TOK;
-      if ((i == 0 || has1) && tok <= t_last[i])
-        out[int64_t(tok) * lay.o_ts + int64_t(kvh * NREP + r / TOK) * lay.o_hs + e % D] = Elem<T>::from_f(0.f);
+      if ((i == 0 || has1) && tok <= t_last[i] && r / TOK < nvh)
+        out[int64_t(tok) * lay.o_ts + int64_t(head0 + r / TOK) * lay.o_hs + e % D] = Elem<T>::from_f(0.f);
     }
     return;
   }
@@ -284,9 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
           for (int g = 0; g < NREP; ++g) {
 #pragma unroll
             for (int h = 0; h < C::kHalves; ++h) {
-              // box = TOK tokens x 64 dims of head kvh * NREP + g (rows past the end read as zeros)
+              // box = TOK tokens x 64 dims of head head0 + g (rows past the end read as zeros)
               tma_load_3d(smem + C::kOffQ + i * C::kQTileBytes + h * kHalfBytes + g * TOK * 128, &qmap, h * 64, t0[i],
-                          kvh * NREP + g, q_full);
+                          head0 + min(g, nvh - 1), q_full);
             }
           }
         }
@@ -412,8 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;  // tile row == TMEM lane
     const int g = r / TOK, tok = t0[i] + r % TOK;
-    const bool row_valid = tok <= t_last[i];
-    const int head = kvh * NREP + g;
+    const bool row_valid = tok <= t_last[i] && g < nvh;
+    const int head = head0 + g;
     int pos = (row_valid && positions) ? __ldg(positions + tok) : p_last[i];
     pos = max(min(pos, kv_len - 1), 0);
     const float scale = kLog2e * rsqrtf(float(D));
@@ -554,16 +561,17 @@ template <typename T, int D, int NREP>
 cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                       int n_kv_heads, int num_seqs, int64_t q_len_flatten, const int32_t* cu_seqlens,
                       const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
-                      const int32_t* positions, const PrefillPlan& plan, const QOLayout& lay, void* workspace,
-                      int* err, cudaStream_t stream) {
+                      const int32_t* positions, const PrefillPlan& plan, const QOLayout& lay, int group,
+                      void* workspace, int* err, cudaStream_t stream) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;
+  const int chunks = (group + NREP - 1) / NREP;
   const CUtensorMapDataType tdt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap qmap, kmap, vmap;
   const uint64_t pool_rows = uint64_t(num_blocks) * n_kv_heads * kPageSize;
   // q as (D, tokens, heads) with the caller's strides: any (T, H, D)-indexable layout.
-  const uint64_t qdims[3] = {uint64_t(D), uint64_t(q_len_flatten), uint64_t(n_kv_heads) * NREP};
+  const uint64_t qdims[3] = {uint64_t(D), uint64_t(q_len_flatten), uint64_t(n_kv_heads) * group};
   const uint64_t qstrides[2] = {uint64_t(lay.q_ts) * 2, uint64_t(lay.q_hs) * 2};
   const uint32_t qbox[3] = {64, uint32_t(TOK), 1};
   cudaError_t ce = make_tma_3d(&qmap, q, tdt, qdims, qstrides, qbox, true);
@@ -578,12 +586,12 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   auto kern = prefill_tc_kernel<T, D, NREP>;
   ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (ce != cudaSuccess) return ce;
-  const int64_t ctas = plan.max_tiles * n_kv_heads;
+  const int64_t ctas = plan.max_tiles * n_kv_heads * chunks;
   if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
   kern<<<unsigned(ctas), kThreads, C::kSmemBytes, stream>>>(qmap, kmap, vmap, static_cast<T*>(out), q_len_flatten,
                                                             num_seqs, n_kv_heads, num_blocks, cu_seqlens, order,
                                                             cu_items, block_tables, max_blocks_per_seq, kv_lens,
-                                                            positions, lay, err);
+                                                            positions, lay, group, chunks, err);
   return cudaGetLastError();
 }
 
@@ -594,18 +602,16 @@ cudaError_t dispatch_tc(int nrep, const void* q, void* out, const void* k_pool, 
                         const int32_t* kv_lens, const int32_t* positions, const PrefillPlan& plan,
                         const QOLayout& lay, void* ws, int* err, cudaStream_t stream) {
 #define FVB_TC_ARGS q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, block_tables, \
-                    max_blocks_per_seq, kv_lens, positions, plan, lay, ws, err, stream
-  switch (nrep) {
+                    max_blocks_per_seq, kv_lens, positions, plan, lay, nrep, ws, err, stream
+  switch (decode_tile_heads(nrep)) {
     case 1:
       return launch_tc<T, D, 1>(FVB_TC_ARGS);
     case 2:
       return launch_tc<T, D, 2>(FVB_TC_ARGS);
     case 4:
       return launch_tc<T, D, 4>(FVB_TC_ARGS);
-    case 8:
-      return launch_tc<T, D, 8>(FVB_TC_ARGS);
     default:
-      return cudaErrorInvalidValue;
+      return launch_tc<T, D, 8>(FVB_TC_ARGS);
   }
 #undef FVB_TC_ARGS
 }
@@ -623,7 +629,7 @@ PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim
     p.ws_bytes = 0;
     return p;
   }
-  p.tile_tokens = kTileM / (n_heads / n_kv_heads);
+  p.tile_tokens = kTileM / decode_tile_heads(n_heads / n_kv_heads);
   // Work items are query-tile pairs; each sequence wastes at most one partial pair.
   p.max_tiles = (q_len_flatten + 2 * p.tile_tokens - 1) / (2 * p.tile_tokens) + num_seqs;
   // order[num_seqs] (padded to 64 entries) + cu_items[num_seqs + 1]

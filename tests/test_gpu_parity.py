@@ -69,9 +69,13 @@ def test_golden_store_then_attend(name, dtype, cuda_device):
 DECODE_LENS = [1, 2, 15, 16, 17, 31, 32, 33, 64, 100, 257, 1000, 2049, 5000]
 
 
+# Group sizes of the Qwen3 family (2, 4, 5 for 14B, 8, 16 for 235B) plus odd ones.
+GQA_SIZES = [1, 2, 3, 4, 5, 6, 8, 16]
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("head_dim", [64, 128])
-@pytest.mark.parametrize("n_rep", [1, 2, 4, 8])
+@pytest.mark.parametrize("n_rep", GQA_SIZES)
 def test_decode_sweep(dtype, head_dim, n_rep, cuda_device):
     hkv = 2
     rng = np.random.default_rng(head_dim * 10 + n_rep)
@@ -108,7 +112,7 @@ PREFILL_CASES = [
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("head_dim", [64, 128])
-@pytest.mark.parametrize("n_rep", [1, 2, 4, 8])
+@pytest.mark.parametrize("n_rep", GQA_SIZES)
 @pytest.mark.parametrize("case", range(len(PREFILL_CASES)))
 def test_prefill_sweep(dtype, head_dim, n_rep, case, cuda_device):
     q_lens, pre = map(np.asarray, PREFILL_CASES[case])

@@ -44,7 +44,7 @@ def _decode_args(**over):
     "over,status",
     [
         (dict(d=96), 2),  # head_dim
-        (dict(hq=6, hkv=2), 2),  # GQA group 3
+        (dict(hq=7, hkv=2), 2),  # heads not a whole number of GQA groups
         (dict(bs=32), 2),  # block size
         (dict(dtype=7), 2),
         (dict(q=8), 3),  # 16-byte rule
