@@ -73,6 +73,15 @@ FVB_API int fvb_max_kv_len(void);
 FVB_API int fvb_read_device_error(int* code, int* info, void* stream);
 
 /*
+ * Diagnostic: launches one thread that waits, through the bounded mbarrier wait all kernels here use,
+ * on a barrier nothing completes.  The wait gives up after its limit (2 s), records
+ * FVB_ERR_DEVICE_TIMEOUT with info = site in the device error word (fvb_read_device_error) and the
+ * kernel ends normally, so the context stays usable.  Shows how a stalled pipeline is reported instead
+ * of hanging the GPU.  No counterpart in the reference.
+ */
+FVB_API int fvb_check_bounded_wait(int site, void* stream);
+
+/*
  * store_kvcache: pool[slot / 16][h][slot % 16][:] = new[t][h][:] for K and V.
  *
  * Replaces the Python KV-write loops of QwenSelfAttention

@@ -156,6 +156,21 @@ cudaError_t make_tma_3d(CUtensorMap* map, const void* base, CUtensorMapDataType 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+namespace {
+// One thread waits, through the same bounded mbar_wait every kernel uses, on a
+// barrier that no thread ever arrives on: the wait must give up after its limit,
+// record FVB_ERR_DEVICE_TIMEOUT with `site` and let the kernel end normally.
+__global__ void bounded_wait_probe_kernel(int* err, int site) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, err, site);
+}
+}  // namespace
+
 }  // namespace fvb
 
 using namespace fvb;
@@ -207,6 +222,14 @@ int fvb_read_device_error(int* code, int* info, void* stream) {
   *info = word[1];
   const int zero[2] = {0, 0};
   return cuda_status(cudaMemcpyToSymbol(g_device_error, zero, sizeof(zero)));
+}
+
+int fvb_check_bounded_wait(int site, void* stream) {
+  cudaError_t e;
+  int* err = device_error_ptr(&e);
+  if (!err) return cuda_status(e);
+  bounded_wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(err, site);
+  return cuda_status(cudaGetLastError());
 }
 
 int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride, void* k_pool,

@@ -40,6 +40,7 @@ _SIGNATURES = {
     "fvb_dim_head": (c_int, []),
     "fvb_max_kv_len": (c_int, []),
     "fvb_read_device_error": (c_int, [ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_void_p]),
+    "fvb_check_bounded_wait": (c_int, [c_int, c_void_p]),
     "fvb_store_kvcache": (
         c_int,
         [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,
