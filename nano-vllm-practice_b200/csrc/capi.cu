@@ -333,9 +333,9 @@ size_t fvb_paged_attention_decode_workspace_size(int num_seqs, int n_heads, int 
   if (num_seqs <= 0 || !gqa_ok(n_heads, n_kv_heads)) return 0;
   const size_t split_ws = plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count()).ws_bytes;
   if (!decode_on_tensor_cores(n_heads, n_kv_heads, FVB_DTYPE_BF16)) return split_ws;
-  // 16-bit GQA >= 8 decodes on the tensor-core path (whose plan does not depend on the
+  // 16-bit GQA >= 5 decodes on the tensor-core path (whose plan does not depend on the
   // dtype); fp32 keeps the split-KV plan.  The size covers both.
-  const size_t tc_ws = plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, num_seqs, 1, FVB_DTYPE_BF16).ws_bytes;
+  const size_t tc_ws = plan_tc_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count()).ws_bytes;
   return split_ws > tc_ws ? split_ws : tc_ws;
 }
 
@@ -367,15 +367,15 @@ int fvb_paged_attention_decode_strided(const void* q, int64_t q_token_stride, in
   if (decode_on_tensor_cores(n_heads, n_kv_heads, dtype)) {
     // One 128-row tile per (sequence, kv head) holds the group's n_rep heads: the
     // tcgen05 attention kernel in decode mode (no cu_seqlens / positions).
-    const PrefillPlan pp = plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, num_seqs, 1, dtype);
-    if (!workspace || workspace_bytes < pp.ws_bytes) return FVB_ERR_WORKSPACE_TOO_SMALL;
+    const TcDecodePlan tp = plan_tc_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count());
+    if (!workspace || workspace_bytes < tp.ws_bytes) return FVB_ERR_WORKSPACE_TOO_SMALL;
     if (reinterpret_cast<uintptr_t>(workspace) & 255) return FVB_ERR_MISALIGNED;
     cudaError_t e;
     int* err = device_error_ptr(&e);
     if (!err) return cuda_status(e);
-    return cuda_status(launch_prefill(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
-                                      num_seqs, nullptr, 1, block_tables, max_blocks_per_seq, kv_lens, nullptr, dtype,
-                                      pp, lay, workspace, err, static_cast<cudaStream_t>(stream)));
+    return cuda_status(launch_tc_decode(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
+                                        block_tables, max_blocks_per_seq, kv_lens, dtype, tp, lay, workspace, err,
+                                        static_cast<cudaStream_t>(stream)));
   }
   const DecodePlan plan = plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count());
   if (plan.ws_bytes > 0 && (!workspace || workspace_bytes < plan.ws_bytes)) return FVB_ERR_WORKSPACE_TOO_SMALL;

@@ -519,4 +519,36 @@ cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const vo
 #undef FVB_DECODE_ARGS
 }
 
+namespace {
+template <typename T, int D>
+cudaError_t launch_combine_t(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens, int kv_cap,
+                             int num_seqs, int n_heads, int pages_per_split, int max_splits, const QOLayout& lay,
+                             cudaStream_t stream) {
+  const size_t csmem = (size_t(max_splits) + D / 32) * sizeof(float);
+  if (csmem > 48 * 1024) {
+    cudaError_t ce =
+        cudaFuncSetAttribute(decode_combine_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(csmem));
+    if (ce != cudaSuccess) return ce;
+  }
+  decode_combine_kernel<T, D><<<unsigned(num_seqs * n_heads), D, csmem, stream>>>(
+      ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap, num_seqs, n_heads, pages_per_split, max_splits, lay);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_decode_combine(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens,
+                                  int kv_cap, int num_seqs, int n_heads, int head_dim, int pages_per_split,
+                                  int max_splits, int dtype, const QOLayout& lay, cudaStream_t stream) {
+  if (num_seqs == 0 || max_splits <= 1) return cudaSuccess;
+#define FVB_CMB_ARGS ws_o, ws_lse, out, kv_lens, kv_cap, num_seqs, n_heads, pages_per_split, max_splits, lay, stream
+  if (dtype == FVB_DTYPE_BF16) {
+    return head_dim == 128 ? launch_combine_t<__nv_bfloat16, 128>(FVB_CMB_ARGS)
+                           : launch_combine_t<__nv_bfloat16, 64>(FVB_CMB_ARGS);
+  } else if (dtype == FVB_DTYPE_F16) {
+    return head_dim == 128 ? launch_combine_t<__half, 128>(FVB_CMB_ARGS) : launch_combine_t<__half, 64>(FVB_CMB_ARGS);
+  }
+  return head_dim == 128 ? launch_combine_t<float, 128>(FVB_CMB_ARGS) : launch_combine_t<float, 64>(FVB_CMB_ARGS);
+#undef FVB_CMB_ARGS
+}
+
 }  // namespace fvb

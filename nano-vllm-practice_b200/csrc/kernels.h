@@ -44,6 +44,9 @@ cudaError_t launch_build_slot_mapping(const int32_t* positions, int64_t num_toke
 // Query heads one decode CTA serves: the GQA group size rounded up to 1, 2, 4 or 8.
 // Larger groups are served in chunks of 8 heads (K/V read once per chunk).
 inline int decode_tile_heads(int group) { return group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8; }
+// Query heads of one 128-row tensor-core tile (128 / heads tokens each): the GQA group
+// rounded up to a power of two, at most 16 (8 tokens, one 1024-byte swizzle atom per head).
+inline int tc_tile_heads(int group) { return group <= 8 ? decode_tile_heads(group) : 16; }
 
 struct DecodePlan {
   int pages_per_split;  // multiple of the 2-page stage
@@ -72,6 +75,26 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
                            int max_blocks_per_seq, const int32_t* kv_lens, const int32_t* positions, int dtype,
                            const PrefillPlan& plan, const QOLayout& lay, void* workspace, int* err,
                            cudaStream_t stream);
+
+// Decode on the tensor-core attention kernel (decode mode: token s of sequence s at
+// position kv_len - 1), with split-KV when there are too few (sequence, kv head) CTAs.
+struct TcDecodePlan {
+  PrefillPlan base;     // one work item per sequence
+  int tiles_per_split;  // 128-key tiles per split; 0 = no split
+  int max_splits;
+  size_t off_o, off_lse;  // fp32 partials [seq][head][split][D] and log2-sum-exps in the workspace
+  size_t ws_bytes;
+};
+TcDecodePlan plan_tc_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int max_kv_len, int num_sms);
+cudaError_t launch_tc_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                             int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
+                             int max_blocks_per_seq, const int32_t* kv_lens, int dtype, const TcDecodePlan& plan,
+                             const QOLayout& lay, void* workspace, int* err, cudaStream_t stream);
+// Merge split partials (decode.cu): sequences with more than one split of
+// pages_per_split pages; the others were written directly.
+cudaError_t launch_decode_combine(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens,
+                                  int kv_cap, int num_seqs, int n_heads, int head_dim, int pages_per_split,
+                                  int max_splits, int dtype, const QOLayout& lay, cudaStream_t stream);
 
 cudaError_t launch_prefill_simt(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                                 int n_heads, int n_kv_heads, int head_dim, int num_seqs, int64_t q_len_flatten,

@@ -183,7 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     int n_kv_heads, int64_t num_blocks, const int32_t* __restrict__ cu_seqlens, const int32_t* __restrict__ order,
     const int32_t* __restrict__ cu_items, const int32_t* __restrict__ block_tables, int max_blocks_per_seq,
     const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, const QOLayout lay, int group,
-    int chunks, int* __restrict__ err) {
+    int chunks, int tiles_per_split, int max_splits, float* __restrict__ ws_o, float* __restrict__ ws_lse,
+    int* __restrict__ err) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;  // query tokens per tile
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -204,8 +205,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   // CTA = (work item, kv head, chunk): a GQA group of `group` query heads is served in
   // chunks of NREP heads (the tile's head slots); slots past the group load a real
   // head's q and are never written.
+  // With split-KV (decode mode, tiles_per_split > 0) each such CTA is further one of
+  // max_splits ranges of 128-key tiles.
+  const int nsp = tiles_per_split > 0 ? max_splits : 1;
+  const int split = int(blockIdx.x) % nsp, cta = int(blockIdx.x) / nsp;
   const int units = n_kv_heads * chunks;
-  const int item = int(blockIdx.x) / units, unit = int(blockIdx.x) % units;
+  const int item = cta / units, unit = cta % units;
   const int kvh = unit / chunks, chunk = unit % chunks;
   const int head0 = kvh * group + chunk * NREP;     // query head of tile slot g = head0 + g
   const int nvh = min(NREP, group - chunk * NREP);  // slots that are real heads
@@ -237,18 +242,32 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     p_last[i] = (live && kv_len > 0) ? max(min(p_tok, kv_len - 1), 0) : -1;
     nkv[i] = p_last[i] >= 0 ? p_last[i] / kTileN + 1 : 0;
   }
-  const int n_kv = max(nkv[0], nkv[1]);
+  int n_kv = max(nkv[0], nkv[1]);
   const int pos_max = max(p_last[0], p_last[1]);  // last key visible to any row of the item
   const int need_pages = pos_max / kPageSize + 1;  // pages holding every visible key
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (n_kv == 0) {  // empty context (never produced by the engine): zeros, not garbage
-    for (int e = threadIdx.x; e < 2 * kTileM * D; e += kThreads) {
+    for (int e = threadIdx.x; split == 0 && e < 2 * kTileM * D; e += kThreads) {
       const int i = e / (kTileM * D), r = (e / D) % kTileM, tok = t0[i] + r % TOK;
       if ((i == 0 || has1) && tok <= t_last[i] && r / TOK < nvh)
         out[int64_t(tok) * lay.o_ts + int64_t(head0 + r / TOK) * lay.o_hs + e % D] = Elem<T>::from_f(0.f);
     }
     return;
+  }
+  // KV tiles of this CTA: [j0, j0 + n_kv) in global tile numbers; the loops below
+  // count j from 0 (ring slots, barrier phases, the softmax's first tile) and add
+  // j0 for page and key offsets.
+  int j0 = 0;
+  bool partial_out = false;  // more than one split: write a normalised partial + log2-sum-exp
+  if (tiles_per_split > 0) {
+    const int ns = (n_kv + tiles_per_split - 1) / tiles_per_split;
+    if (split >= ns) return;  // this split lies past the sequence (uniform per CTA)
+    j0 = split * tiles_per_split;
+    partial_out = ns > 1;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) nkv[i] = max(0, min(nkv[i], j0 + tiles_per_split) - j0);
+    n_kv = max(nkv[0], nkv[1]);
   }
 
   if (threadIdx.x == 0) {
@@ -306,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       const int32_t* table = block_tables + int64_t(s) * max_blocks_per_seq;
       for (int j = 0; j < n_kv; ++j) {
         const int st = j % nst_ring, use = j / nst_ring;
-        const int p0 = j * (kTileN / kPageSize);
+        const int p0 = (j0 + j) * (kTileN / kPageSize);
         const int np = min(kTileN / kPageSize, need_pages - p0);
         int rows[kTileN / kPageSize];
         for (int pi = 0; pi < np; ++pi) {
@@ -435,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       tc_fence_after();
       uint32_t sr[128];
       tmem_ld_128cols(t_row + col_s(i), sr);
-      const int kbase = j * kTileN;
+      const int kbase = (j0 + j) * kTileN;
       if (kbase + kTileN - 1 > pos) {
 #pragma unroll
         for (int c = 0; c < 128; ++c) {
@@ -529,11 +548,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       tc_fence_after();
       const float inv_l = 1.f / l;
       T* orow = out + int64_t(tok) * lay.o_ts + int64_t(head) * lay.o_hs;
+      // split partial of (sequence tok, head): O / l in fp32 and log2(sum exp) in log2 units,
+      // the layout decode_combine_kernel merges ([seq][head][split][D], [seq][head][split])
+      const int64_t pidx = (int64_t(tok) * (n_kv_heads * group) + head) * max_splits + split;
+      if (partial_out && row_valid) ws_lse[pidx] = m_ref * scale + __log2f(l);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t o[32];
         tmem_ld_32cols(t_row + col_o(i) + cc * 32, o);
-        if (row_valid) {
+        if (partial_out) {
+          if (row_valid) {
+            float4* dst = reinterpret_cast<float4*>(ws_o + pidx * D + cc * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              dst[q] = make_float4(__uint_as_float(o[q * 4 + 0]) * inv_l, __uint_as_float(o[q * 4 + 1]) * inv_l,
+                                   __uint_as_float(o[q * 4 + 2]) * inv_l, __uint_as_float(o[q * 4 + 3]) * inv_l);
+          }
+        } else if (row_valid) {
           uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -562,7 +593,8 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
                       int n_kv_heads, int num_seqs, int64_t q_len_flatten, const int32_t* cu_seqlens,
                       const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
                       const int32_t* positions, const PrefillPlan& plan, const QOLayout& lay, int group,
-                      void* workspace, int* err, cudaStream_t stream) {
+                      int tiles_per_split, int max_splits, float* ws_o, float* ws_lse, void* workspace, int* err,
+                      cudaStream_t stream) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;
   const int chunks = (group + NREP - 1) / NREP;
@@ -586,12 +618,13 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   auto kern = prefill_tc_kernel<T, D, NREP>;
   ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (ce != cudaSuccess) return ce;
-  const int64_t ctas = plan.max_tiles * n_kv_heads * chunks;
+  const int64_t ctas = plan.max_tiles * n_kv_heads * chunks * (tiles_per_split > 0 ? max_splits : 1);
   if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
   kern<<<unsigned(ctas), kThreads, C::kSmemBytes, stream>>>(qmap, kmap, vmap, static_cast<T*>(out), q_len_flatten,
                                                             num_seqs, n_kv_heads, num_blocks, cu_seqlens, order,
                                                             cu_items, block_tables, max_blocks_per_seq, kv_lens,
-                                                            positions, lay, group, chunks, err);
+                                                            positions, lay, group, chunks, tiles_per_split,
+                                                            max_splits, ws_o, ws_lse, err);
   return cudaGetLastError();
 }
 
@@ -600,18 +633,22 @@ cudaError_t dispatch_tc(int nrep, const void* q, void* out, const void* k_pool, 
                         int64_t num_blocks, int n_kv_heads, int num_seqs, int64_t q_len_flatten,
                         const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
                         const int32_t* kv_lens, const int32_t* positions, const PrefillPlan& plan,
-                        const QOLayout& lay, void* ws, int* err, cudaStream_t stream) {
+                        const QOLayout& lay, int tiles_per_split, int max_splits, float* ws_o, float* ws_lse, void* ws,
+                        int* err, cudaStream_t stream) {
 #define FVB_TC_ARGS q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, block_tables, \
-                    max_blocks_per_seq, kv_lens, positions, plan, lay, nrep, ws, err, stream
-  switch (decode_tile_heads(nrep)) {
+                    max_blocks_per_seq, kv_lens, positions, plan, lay, nrep, tiles_per_split, max_splits, ws_o,    \
+                    ws_lse, ws, err, stream
+  switch (tc_tile_heads(nrep)) {
     case 1:
       return launch_tc<T, D, 1>(FVB_TC_ARGS);
     case 2:
       return launch_tc<T, D, 2>(FVB_TC_ARGS);
     case 4:
       return launch_tc<T, D, 4>(FVB_TC_ARGS);
-    default:
+    case 8:
       return launch_tc<T, D, 8>(FVB_TC_ARGS);
+    default:
+      return launch_tc<T, D, 16>(FVB_TC_ARGS);
   }
 #undef FVB_TC_ARGS
 }
@@ -629,7 +666,7 @@ PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim
     p.ws_bytes = 0;
     return p;
   }
-  p.tile_tokens = kTileM / decode_tile_heads(n_heads / n_kv_heads);
+  p.tile_tokens = kTileM / tc_tile_heads(n_heads / n_kv_heads);
   // Work items are query-tile pairs; each sequence wastes at most one partial pair.
   p.max_tiles = (q_len_flatten + 2 * p.tile_tokens - 1) / (2 * p.tile_tokens) + num_seqs;
   // order[num_seqs] (padded to 64 entries) + cu_items[num_seqs + 1]
@@ -647,13 +684,71 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
   if (num_seqs == 0 || q_len_flatten == 0) return cudaSuccess;
   const int nrep = n_heads / n_kv_heads;
 #define FVB_DISPATCH_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, \
-                          block_tables, max_blocks_per_seq, kv_lens, positions, plan, lay, workspace, err, stream
+                          block_tables, max_blocks_per_seq, kv_lens, positions, plan, lay, 0, 1, nullptr, nullptr, \
+                          workspace, err, stream
   if (dtype == FVB_DTYPE_BF16) {
     return head_dim == 128 ? dispatch_tc<__nv_bfloat16, 128>(FVB_DISPATCH_ARGS)
                            : dispatch_tc<__nv_bfloat16, 64>(FVB_DISPATCH_ARGS);
   }
   return head_dim == 128 ? dispatch_tc<__half, 128>(FVB_DISPATCH_ARGS) : dispatch_tc<__half, 64>(FVB_DISPATCH_ARGS);
 #undef FVB_DISPATCH_ARGS
+}
+
+TcDecodePlan plan_tc_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int max_kv_len, int num_sms) {
+  TcDecodePlan p{};
+  p.base = plan_prefill(num_seqs, n_heads, n_kv_heads, head_dim, num_seqs, 1, FVB_DTYPE_BF16);
+  p.tiles_per_split = 0;
+  p.max_splits = 1;
+  p.ws_bytes = p.base.ws_bytes;
+  if (num_seqs <= 0 || n_kv_heads <= 0) return p;
+  const int group = n_heads / n_kv_heads, tile = tc_tile_heads(group);
+  const int64_t ctas = int64_t(num_seqs) * n_kv_heads * ((group + tile - 1) / tile);
+  const int kv_tiles = std::max(1, (max_kv_len + kTileN - 1) / kTileN);
+  // One resident CTA per SM (TMEM and shared memory): split the KV range until there
+  // are about two waves, keeping at least 4 tiles (512 keys) per split.
+  const int64_t target = int64_t(num_sms) * 2;
+  if (ctas >= target || kv_tiles < 8) return p;
+  int splits = int(std::min<int64_t>((target + ctas - 1) / ctas, kv_tiles / 4));
+  if (splits <= 1) return p;
+  const int tps = (kv_tiles + splits - 1) / splits;
+  splits = (kv_tiles + tps - 1) / tps;
+  if (splits <= 1) return p;
+  p.tiles_per_split = tps;
+  p.max_splits = splits;
+  const size_t rows = size_t(num_seqs) * n_heads * splits;
+  p.off_o = p.base.ws_bytes;
+  p.off_lse = p.off_o + ((rows * head_dim * 4 + 255) & ~size_t(255));
+  p.ws_bytes = p.off_lse + rows * 4;
+  return p;
+}
+
+cudaError_t launch_tc_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                             int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
+                             int max_blocks_per_seq, const int32_t* kv_lens, int dtype, const TcDecodePlan& plan,
+                             const QOLayout& lay, void* workspace, int* err, cudaStream_t stream) {
+  if (num_seqs == 0) return cudaSuccess;
+  const int nrep = n_heads / n_kv_heads;
+  float* ws_o = nullptr;
+  float* ws_lse = nullptr;
+  if (plan.tiles_per_split > 0) {
+    ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.off_o);
+    ws_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.off_lse);
+  }
+  // decode mode: no cu_seqlens / positions (token s = sequence s at position kv_len - 1)
+#define FVB_TCD_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, int64_t(num_seqs), nullptr, \
+                     block_tables, max_blocks_per_seq, kv_lens, nullptr, plan.base, lay, plan.tiles_per_split,    \
+                     plan.max_splits, ws_o, ws_lse, workspace, err, stream
+  cudaError_t ce;
+  if (dtype == FVB_DTYPE_BF16) {
+    ce = head_dim == 128 ? dispatch_tc<__nv_bfloat16, 128>(FVB_TCD_ARGS) : dispatch_tc<__nv_bfloat16, 64>(FVB_TCD_ARGS);
+  } else {
+    ce = head_dim == 128 ? dispatch_tc<__half, 128>(FVB_TCD_ARGS) : dispatch_tc<__half, 64>(FVB_TCD_ARGS);
+  }
+#undef FVB_TCD_ARGS
+  if (ce != cudaSuccess || plan.tiles_per_split == 0) return ce;
+  return launch_decode_combine(ws_o, ws_lse, out, kv_lens, max_blocks_per_seq * kPageSize, num_seqs, n_heads,
+                               head_dim, plan.tiles_per_split * (kTileN / kPageSize), plan.max_splits, dtype, lay,
+                               stream);
 }
 
 }  // namespace fvb
