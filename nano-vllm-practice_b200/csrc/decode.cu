@@ -212,7 +212,6 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t qs_addr = smem_u32(qs);
   float* pw = ps + cw * kStageTokens * NREP;
-  const uint32_t pw_addr = smem_u32(pw);
   // Lane-constant part of this lane's K row address inside a slot.
   const int kr = lane & 15;
   const uint32_t k_lane_off = (lane >> 4) * Tr::kPageBytes + kr * 128;
@@ -308,8 +307,6 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
-  (void)pw_addr;
-  (void)qs_addr;
 
   // ---------------- merge the four warps ----------------
   named_barrier(1, 32 * kConsumerWarps);  // every consumer is done with the ring
