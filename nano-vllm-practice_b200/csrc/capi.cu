@@ -2,6 +2,7 @@
 // include/femtovllm_b200.h).  Host-side validation of every scalar argument,
 // the 16-byte alignment rules of the TMA / vector paths, workspace sizing,
 // and mapping of CUDA errors to fvb_status.  Nothing here allocates.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 
@@ -16,9 +17,11 @@ __device__ int g_device_error[2] = {0, 0};
 namespace {
 
 constexpr int kMaxDevices = 64;
-int* g_err_ptr[kMaxDevices] = {};
+std::atomic<int*> g_err_ptr[kMaxDevices] = {};
 
-// Device address of g_device_error on the current device (resolved once per device).
+// Device address of g_device_error on the current device, resolved once per device.
+// Threads racing on the first call all resolve the same address; the atomic keeps the
+// cache itself race-free.
 int* device_error_ptr(cudaError_t* e) {
   int dev = 0;
   *e = cudaGetDevice(&dev);
@@ -27,13 +30,15 @@ int* device_error_ptr(cudaError_t* e) {
     *e = cudaErrorInvalidDevice;
     return nullptr;
   }
-  if (!g_err_ptr[dev]) {
+  int* cached = g_err_ptr[dev].load(std::memory_order_acquire);
+  if (!cached) {
     void* p = nullptr;
     *e = cudaGetSymbolAddress(&p, g_device_error);
     if (*e != cudaSuccess) return nullptr;
-    g_err_ptr[dev] = static_cast<int*>(p);
+    cached = static_cast<int*>(p);
+    g_err_ptr[dev].store(cached, std::memory_order_release);
   }
-  return g_err_ptr[dev];
+  return cached;
 }
 
 thread_local int t_last_cuda_error = 0;
@@ -112,16 +117,18 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 namespace {
 cudaError_t tensor_map_encoder(EncodeTiledFn* out) {
-  static EncodeTiledFn encode = nullptr;
-  if (!encode) {
+  static std::atomic<EncodeTiledFn> encode{nullptr};  // resolved once; concurrent first calls agree
+  EncodeTiledFn fnp = encode.load(std::memory_order_acquire);
+  if (!fnp) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult qres;
     cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &qres);
     if (e != cudaSuccess) return e;
     if (qres != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-    encode = reinterpret_cast<EncodeTiledFn>(fn);
+    fnp = reinterpret_cast<EncodeTiledFn>(fn);
+    encode.store(fnp, std::memory_order_release);
   }
-  *out = encode;
+  *out = fnp;
   return cudaSuccess;
 }
 }  // namespace

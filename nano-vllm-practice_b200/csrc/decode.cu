@@ -422,7 +422,7 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
                                 Tr::kRowBytes, Tr::kBoxCols, kPageSize, true);
   if (ce != cudaSuccess) return ce;
   auto kern = decode_split_kernel<T, D, NREP>;
-  ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  ce = set_smem_once<decode_split_kernel<T, D, NREP>>(Tr::kSmemBytes);
   if (ce != cudaSuccess) return ce;
   float* ws_o = nullptr;
   float* ws_lse = nullptr;

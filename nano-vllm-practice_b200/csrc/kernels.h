@@ -6,7 +6,24 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace fvb {
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize, bytes) for kernel Kern once per
+// device (bytes is fixed per kernel), keeping the driver call off every launch.
+template <auto Kern>
+cudaError_t set_smem_once(int bytes) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return ce;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  ce = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (ce == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return ce;
+}
 
 // Host-side encoder for 2-D tiled TMA descriptors (cuTensorMapEncodeTiled,
 // resolved through the runtime's driver entry point so nothing links libcuda).

@@ -616,7 +616,7 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   ce = cudaGetLastError();
   if (ce != cudaSuccess) return ce;
   auto kern = prefill_tc_kernel<T, D, NREP>;
-  ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  ce = set_smem_once<prefill_tc_kernel<T, D, NREP>>(C::kSmemBytes);
   if (ce != cudaSuccess) return ce;
   const int64_t ctas = plan.max_tiles * n_kv_heads * chunks * (tiles_per_split > 0 ? max_splits : 1);
   if (ctas > 0x7fffffff) return cudaErrorInvalidValue;
