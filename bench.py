@@ -318,11 +318,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seqs", type=int, default=24)
     ap.add_argument("--num-seqs", type=int, default=256, help="sequences per GPU (256 = BASELINE config 2)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long", "qk_norm_rope", "decode_graph"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long", "qk_norm_rope", "decode_graph", "store"],
                     help="decode = config 2 (the contract line); prefill = config 3; mixed = config 4; "
                          "long = config 5 sharded over the ranks; qk_norm_rope = the fused q/k norm + rotary + "
                          "KV write over config 3's new tokens; decode_graph = one small-batch decode step "
-                         "(slots + fused norm/rope/write + attention) eager vs replayed from a CUDA graph")
+                         "(slots + fused norm/rope/write + attention) eager vs replayed from a CUDA graph; "
+                         "store = store_kvcache of 65,536 new tokens (config 2's heads)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -346,6 +347,9 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
     if args.workload == "decode_graph":
         run_decode_graph(args, rank, local_rank)
+        return
+    if args.workload == "store":
+        run_store(args, rank, local_rank, hbm_peak, peak_src)
         return
     if args.workload != "decode":
         run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src)
@@ -502,6 +506,52 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
             "pct_tensor_peak": round(100 * flops / (t * 1e-3) / 1e12 / (tflops_peak * world), 2),
             "pct_hbm_peak": round(100 * nbytes / (t * 1e-3) / 1e9 / (hbm_peak * world), 2),
             "peak_source": peak_src, "config": batch.name, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
+def run_store(args, rank, local_rank, hbm_peak, peak_src):
+    """store_kvcache alone at prefill size: T new tokens (65,536 unless --num-seqs gives another T) of
+    config 2's heads (Hkv 8, D 128, bf16) scattered through a random slot mapping into a pool with room
+    for 2 T tokens.  Inputs and pool exceed L2."""
+    import numpy as np
+    import torch
+
+    from femtovllm_b200 import ops
+
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T = args.num_seqs if args.num_seqs != 256 else 65536
+    hkv, D = 8, 128
+    g = torch.Generator(device=dev).manual_seed(11)
+    k = torch.randn(T, hkv, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(T, hkv, D, generator=g, device=dev).to(torch.bfloat16)
+    blocks = (2 * T + 15) // 16
+    k_pool = torch.zeros(blocks, hkv, 16, D, device=dev, dtype=torch.bfloat16)
+    v_pool = torch.zeros_like(k_pool)
+    rng = np.random.default_rng(11)
+    slots = torch.from_numpy(rng.permutation(blocks * 16)[:T].astype(np.int64)).to(dev)
+
+    def step():
+        ops.store_kvcache(k, v, k_pool, v_pool, slots)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = 2 * 2 * T * hkv * D * 2 + 8 * T  # K and V rows read and written, slots read
+    line = {"metric": "store_kvcache GB/s", "workload": "store", "tokens": T, "n_kv_heads": hkv, "head_dim": D,
+            "steps": args.steps, "ms_per_step": round(ms, 5), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "pct_hbm_peak": round(100 * nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 2), "peak_source": peak_src,
+            "data": "synthetic (seeded N(0,1), random slot permutation)", "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
 
 

@@ -9,12 +9,21 @@
 // group of lanes copies with one coalesced load and one coalesced store each.
 // HBM-bound: 2 * T * Hkv * D * sizeof(T) bytes read and written, plus 8 T
 // bytes of slot_mapping.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace fvb {
 
 // VEC_BYTES = 16 on the aligned path, sizeof(elem) otherwise.
+//
+// Work split: a token has R = 2 * n_kv_heads rows (K rows, then V rows) of
+// L = row_bytes / VEC_BYTES lanes.  Thread tid of a block owns lane tid % L of
+// row slot tid / L for the whole launch: with R * L <= threads a block pass
+// covers threads / (R * L) whole tokens, otherwise one token with each thread
+// taking rows slot, slot + threads / L, ...  Tokens advance by a block-uniform
+// stride, two per step so two loads are in flight; no division in the loop.
 template <int VEC_BYTES>
 __global__ void __launch_bounds__(256) store_kvcache_kernel(const uint8_t* __restrict__ k,
                                                             const uint8_t* __restrict__ v,
@@ -28,31 +37,55 @@ __global__ void __launch_bounds__(256) store_kvcache_kernel(const uint8_t* __res
       VEC_BYTES == 16, uint4,
       typename std::conditional<VEC_BYTES == 8, uint2,
                                 typename std::conditional<VEC_BYTES == 4, uint32_t, uint16_t>::type>::type>::type;
-  const int vecs_per_row = row_bytes / VEC_BYTES;
-  // Work item = (token, kv head, K-or-V, vector); K and V of a row are
-  // adjacent items so one warp streams both.
-  const int64_t items_per_token = int64_t(n_kv_heads) * 2 * vecs_per_row;
-  const int64_t total = num_tokens * items_per_token;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t t = i / items_per_token;
-    int rem = int(i - t * items_per_token);
-    const int h = rem / (2 * vecs_per_row);
-    rem -= h * 2 * vecs_per_row;
-    const int which = rem / vecs_per_row;  // 0 = K, 1 = V
-    const int vec = rem - which * vecs_per_row;
-    const int64_t slot = __ldg(slot_mapping + t);
-    if (slot < 0) continue;  // padding token
-    if (slot >= num_slots) {
-      record_error(err, FVB_ERR_BAD_SLOT, int(t));
-      continue;
-    }
+  const int L = row_bytes / VEC_BYTES;            // vectors per row
+  const int Lb = min(L, int(blockDim.x));          // lanes per row slot (rows wider than a block loop)
+  const int R = 2 * n_kv_heads;                    // rows per token
+  const int slots_pb = int(blockDim.x) / Lb;       // row slots per block
+  const int tid = int(threadIdx.x);
+  const int lane = tid % Lb, slot_id = tid / Lb;
+  if (slot_id >= slots_pb) return;  // the block's last partial row group (L does not divide blockDim.x)
+  const bool packed = R <= slots_pb;
+  const int tpb = packed ? slots_pb / R : 1;  // tokens per block pass
+  if (packed && slot_id >= tpb * R) return;  // spare row slots
+  const int tok_off = packed ? slot_id / R : 0;
+  const int row0 = packed ? slot_id % R : slot_id;
+  const int row_step = packed ? R : slots_pb;
+  const int64_t tstride = int64_t(gridDim.x) * tpb;
+  auto src_of = [&](int64_t t, int row, int ln) -> const Vec* {
+    const int h = row < n_kv_heads ? row : row - n_kv_heads;
+    return reinterpret_cast<const Vec*>((row < n_kv_heads ? k : v) + t * token_stride_b + h * head_stride_b +
+                                        int64_t(ln) * VEC_BYTES);
+  };
+  auto dst_of = [&](int64_t slot, int row, int ln) -> Vec* {
+    const int h = row < n_kv_heads ? row : row - n_kv_heads;
     const int64_t blk = slot / block_size;
     const int off = int(slot - blk * block_size);
-    const uint8_t* src = (which ? v : k) + t * token_stride_b + h * head_stride_b + int64_t(vec) * VEC_BYTES;
-    uint8_t* dst = (which ? v_pool : k_pool) + ((blk * n_kv_heads + h) * block_size + off) * int64_t(row_bytes) +
-                   int64_t(vec) * VEC_BYTES;
-    *reinterpret_cast<Vec*>(dst) = *reinterpret_cast<const Vec*>(src);
+    return reinterpret_cast<Vec*>((row < n_kv_heads ? k_pool : v_pool) +
+                                  ((blk * n_kv_heads + h) * block_size + off) * int64_t(row_bytes) +
+                                  int64_t(ln) * VEC_BYTES);
+  };
+  for (int64_t t = int64_t(blockIdx.x) * tpb + tok_off; t < num_tokens; t += 2 * tstride) {
+    const int64_t t2 = t + tstride;
+    const bool has2 = t2 < num_tokens;
+    int64_t s1 = __ldg(slot_mapping + t);
+    int64_t s2 = has2 ? __ldg(slot_mapping + t2) : -1;
+    if (s1 >= num_slots) {
+      if (row0 == 0 && lane == 0) record_error(err, FVB_ERR_BAD_SLOT, int(t));
+      s1 = -1;
+    }
+    if (s2 >= num_slots) {
+      if (row0 == 0 && lane == 0) record_error(err, FVB_ERR_BAD_SLOT, int(t2));
+      s2 = -1;
+    }
+    for (int row = row0; row < R; row += row_step) {
+      for (int ln = lane; ln < L; ln += Lb) {
+        const Vec a = *src_of(t, row, ln);
+        Vec b{};
+        if (has2) b = *src_of(t2, row, ln);
+        if (s1 >= 0) *dst_of(s1, row, ln) = a;  // -1: padding token, skipped
+        if (s2 >= 0) *dst_of(s2, row, ln) = b;
+      }
+    }
   }
 }
 
@@ -72,14 +105,13 @@ cudaError_t launch_store_kvcache(const void* k, const void* v, int64_t token_str
       break;
     }
   }
-  const int64_t items = num_tokens * n_kv_heads * 2 * (row_bytes / vec_bytes);
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int threads = 256;
-  int64_t blocks = (items + threads - 1) / threads;
-  const int64_t cap = int64_t(sms) * 8;  // grid-stride beyond 8 resident CTAs per SM
+  // grid: enough blocks for every token once (two per step), capped at 8 resident CTAs per SM
+  const int lanes = std::min(row_bytes / vec_bytes, 256), slots_pb = 256 / lanes, rows = 2 * n_kv_heads;
+  const int64_t tpb = rows <= slots_pb ? slots_pb / rows : 1;
+  int64_t blocks = (num_tokens + 2 * tpb - 1) / (2 * tpb);
+  const int64_t cap = int64_t(device_sm_count()) * 8;
   if (blocks > cap) blocks = cap;
+  const int threads = 256;
   const int64_t num_slots = num_blocks * block_size;
   auto* kb = static_cast<const uint8_t*>(k);
   auto* vb = static_cast<const uint8_t*>(v);
