@@ -318,12 +318,14 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seqs", type=int, default=24)
     ap.add_argument("--num-seqs", type=int, default=256, help="sequences per GPU (256 = BASELINE config 2)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long", "qk_norm_rope", "decode_graph", "store"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "mixed", "long", "qk_norm_rope", "decode_graph", "store",
+                                                       "sampler"],
                     help="decode = config 2 (the contract line); prefill = config 3; mixed = config 4; "
                          "long = config 5 sharded over the ranks; qk_norm_rope = the fused q/k norm + rotary + "
                          "KV write over config 3's new tokens; decode_graph = one small-batch decode step "
                          "(slots + fused norm/rope/write + attention) eager vs replayed from a CUDA graph; "
-                         "store = store_kvcache of 65,536 new tokens (config 2's heads)")
+                         "store = store_kvcache of 65,536 new tokens (config 2's heads); "
+                         "sampler = next-token sampling of 256 rows of a 151,936-token vocabulary")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -350,6 +352,9 @@ def main():
         return
     if args.workload == "store":
         run_store(args, rank, local_rank, hbm_peak, peak_src)
+        return
+    if args.workload == "sampler":
+        run_sampler(args, rank, local_rank, hbm_peak, peak_src)
         return
     if args.workload != "decode":
         run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src)
@@ -552,6 +557,76 @@ def run_store(args, rank, local_rank, hbm_peak, peak_src):
             "steps": args.steps, "ms_per_step": round(ms, 5), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
             "pct_hbm_peak": round(100 * nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 2), "peak_source": peak_src,
             "data": "synthetic (seeded N(0,1), random slot permutation)", "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
+def _reference_sampler_ops(logits, temps, pens, table):
+    """The tensor ops of the reference's Sampler.forward (femtovllm/engine/sampler.py:56-109) for a
+    batch whose rows all sample with a presence penalty, restated with torch on the same device
+    tensors: (B, vocab + 1) count matrix by scatter_add, penalty, in-place division, softmax,
+    multinomial.  Timed beside the fused kernel; its host list building is not included."""
+    import torch
+
+    B, V = logits.shape
+    counts = torch.zeros((B, V + 1), dtype=torch.long, device=logits.device)
+    counts.scatter_add_(dim=1, index=table, src=torch.ones_like(table))
+    x = logits - pens[:, None] * (counts[:, :V] > 0)
+    x /= temps[:, None]
+    return torch.multinomial(torch.softmax(x, dim=-1), num_samples=1).squeeze(-1)
+
+
+def run_sampler(args, rank, local_rank, hbm_peak, peak_src):
+    """Next-token sampling of a decode batch: B = 256 rows (config 2's batch) of Qwen3's 151,936-entry
+    vocabulary in bf16, the reference's default SamplingParams (temperature 1.0, presence penalty 1.0)
+    and token histories of config 2's context lengths U[512, 4096].  Four logits buffers are rotated
+    (311 MB > L2).  Algorithmic bytes: the logits once, the token tables once, ids written."""
+    import numpy as np
+    import torch
+
+    from femtovllm_b200 import ops
+
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B = args.num_seqs
+    V = 151936
+    g = torch.Generator(device=dev).manual_seed(21)
+    bufs = [(torch.randn(B, V, generator=g, device=dev) * 3).to(torch.bfloat16) for _ in range(4)]
+    rng = np.random.default_rng(21)
+    lens = rng.integers(512, 4097, B)
+    table_h = np.full((B, int(lens.max())), V, np.int64)
+    for b in range(B):
+        table_h[b, : lens[b]] = rng.integers(0, V, lens[b])
+    table = torch.from_numpy(table_h).to(dev)
+    temps = torch.ones(B, device=dev)
+    pens = torch.ones(B, device=dev)
+    state = ops.new_rng_state(7, dev)
+    ws = ops.sample_workspace(B, V, dev)
+    steps = min(args.steps, 200)
+
+    def timed(fn):
+        for i in range(max(args.warmup, 3)):
+            fn(bufs[i % 4])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            fn(bufs[i % 4])
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    with ClockSampler(local_rank) as clk:
+        ms = timed(lambda lg: ops.sample_tokens(lg, temps, pens, table, state, ws))
+    ms_ref = timed(lambda lg: _reference_sampler_ops(lg, temps, pens, table))
+    nbytes = B * V * 2 + int(table.numel()) * 8 + B * (4 + 4 + 8)
+    line = {"metric": "sampler GB/s", "workload": "sampler", "rows": B, "vocab": V, "dtype": "bf16",
+            "table_len": int(table.shape[1]), "steps": steps, "ms_per_step": round(ms, 5),
+            "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "pct_hbm_peak": round(100 * nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 2), "peak_source": peak_src,
+            "reference_ops_ms_per_step": round(ms_ref, 5), "speedup_vs_reference_ops": round(ms_ref / ms, 2),
+            "data": "synthetic (seeded N(0, 9) bf16 logits, uniform token histories)", "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
 
 

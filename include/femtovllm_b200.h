@@ -97,6 +97,33 @@ FVB_API int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride
                       void* stream);
 
 /*
+ * Next-token sampling over num_rows logit rows in one launch: the reference's Sampler.forward
+ * (femtovllm/engine/sampler.py:15-114), which the model runner calls on lm_head's output
+ * (femtovllm/engine/model_runner.py:150-157).  Row b: logits[b * row_stride + i], i < vocab.
+ *   apply = any |presence_penalties[r]| > 1e-5 over all rows (sampler.py:31-35);
+ *   x[i] = logits[b][i] - presence_penalties[b] if apply and token i occurs in
+ *          token_table[b][0 .. table_len) (entries outside [0, vocab) are padding, the reference
+ *          pads with vocab), else logits[b][i]                          (sampler.py:56-76)
+ *   temperatures[b] < 1e-5: token_ids[b] = first index of the maximum of x  (torch.argmax, :88-95)
+ *   otherwise: token_ids[b] drawn from softmax(x / temperatures[b])         (:97-109), by inverse CDF
+ *          over vocabulary order with the uniform of Philox4x32-10(key = rng_state[0],
+ *          counter = {b, 0, rng_state[1]}); x / T is rounded to the logits' dtype when !apply, as the
+ *          reference's in-place division of 16-bit logits does.
+ * presence_penalties may be NULL (no penalty); token_table int64 [num_rows][table_stride].
+ * rng_state: device uint64[2] {seed, offset}; each launch adds 1 to offset, on the device.
+ * workspace: fvb_sample_workspace_size(num_rows, vocab) bytes, 16-byte aligned; its counters must be
+ * zero before the first launch (e.g. cudaMemsetAsync once) and every launch leaves them zero.
+ * Replaces the reference's Python lists, count matrix and per-group launches; no counterpart in its
+ * native module.
+ */
+FVB_API size_t fvb_sample_workspace_size(int num_rows, int64_t vocab);
+FVB_API int fvb_sample_tokens(const void* logits, int64_t row_stride, int num_rows, int64_t vocab, int dtype,
+                              const float* temperatures, const float* presence_penalties,
+                              const int64_t* token_table, int64_t table_stride, int64_t table_len,
+                              uint64_t* rng_state, int64_t* token_ids, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/*
  * slot_mapping[t] = block_tables[s][positions[t] / 16] * 16 + positions[t] % 16 for every
  * token t of sequence s (cu_seqlens[s] <= t < cu_seqlens[s+1]); -1 where the table entry
  * is -1 (the token is then skipped by fvb_store_kvcache).  cu_seqlens may be NULL for one

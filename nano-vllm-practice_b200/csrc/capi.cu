@@ -320,6 +320,36 @@ int fvb_qk_norm_rope_store(const void* q, int64_t q_token_stride, int64_t q_head
       static_cast<cudaStream_t>(stream)));
 }
 
+size_t fvb_sample_workspace_size(int num_rows, int64_t vocab) {
+  if (num_rows <= 0 || vocab <= 0) return 0;
+  return sample_workspace_size(num_rows, vocab);
+}
+
+int fvb_sample_tokens(const void* logits, int64_t row_stride, int num_rows, int64_t vocab, int dtype,
+                      const float* temperatures, const float* presence_penalties, const int64_t* token_table,
+                      int64_t table_stride, int64_t table_len, uint64_t* rng_state, int64_t* token_ids,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  const int es = esize_of(dtype);
+  if (es == 0) return FVB_ERR_UNSUPPORTED;
+  if (num_rows < 0 || vocab <= 0 || vocab >= (int64_t(1) << 31) || row_stride < vocab || table_len < 0 ||
+      (table_len > 0 && (token_table == nullptr || table_stride < table_len)))
+    return FVB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return FVB_OK;
+  if (int64_t(num_rows) * ((vocab + 2047) / 2048) >= (int64_t(1) << 31)) return FVB_ERR_INVALID_ARGUMENT;
+  if (!logits || !temperatures || !rng_state || !token_ids || !workspace) return FVB_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < sample_workspace_size(num_rows, vocab)) return FVB_ERR_WORKSPACE_TOO_SMALL;
+  if ((reinterpret_cast<uintptr_t>(logits) % es) != 0 || !aligned16(workspace) ||
+      (reinterpret_cast<uintptr_t>(rng_state) & 7) != 0 || (reinterpret_cast<uintptr_t>(token_ids) & 7) != 0 ||
+      (reinterpret_cast<uintptr_t>(temperatures) & 3) != 0 ||
+      (reinterpret_cast<uintptr_t>(presence_penalties) & 3) != 0 ||
+      (reinterpret_cast<uintptr_t>(token_table) & 7) != 0)
+    return FVB_ERR_MISALIGNED;
+  return cuda_status(launch_sample(logits, row_stride, num_rows, vocab, dtype, temperatures, presence_penalties,
+                                   token_table, table_stride, table_len,
+                                   reinterpret_cast<unsigned long long*>(rng_state), token_ids, workspace,
+                                   static_cast<cudaStream_t>(stream)));
+}
+
 int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const int32_t* cu_seqlens, int num_seqs,
                            const int32_t* block_tables, int max_blocks_per_seq, int block_size,
                            int64_t* slot_mapping, void* stream) {

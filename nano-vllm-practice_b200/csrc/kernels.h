@@ -136,6 +136,14 @@ cudaError_t launch_build_varlen_metadata(const int32_t* num_computed, const int3
                                          int32_t* cu_seqlens, int32_t* kv_lens, int32_t* block_tables,
                                          int64_t* slot_mapping, int* err, cudaStream_t stream);
 
+// Next-token sampling (sampler.cu): presence penalty, greedy argmax, temperature
+// sampling; workspace counters zero before the first launch and left zero after each.
+size_t sample_workspace_size(int num_rows, int64_t vocab);
+cudaError_t launch_sample(const void* logits, int64_t row_stride, int num_rows, int64_t vocab, int dtype,
+                          const float* temps, const float* pens, const int64_t* table, int64_t table_stride,
+                          int64_t table_len, unsigned long long* rng, int64_t* out, void* workspace,
+                          cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace fvb

@@ -4,9 +4,9 @@
 // the same entry-point names and argument order (PagedAttentionGemvCuda,
 // PagedAttentionGemmCuda) and the same attributes (kMaxKVLenNonSplit,
 // kKVLenPerPage, kDimHead), plus StoreKVCacheCuda for the slot-mapped KV write
-// the reference does in Python and QKNormRopeStoreCuda for the fused q/k
-// norm + rotary embedding + KV write.  Each function validates like the reference's
-// TORCH_CHECKs (csrc/paged_attention/paged_attention_gemv.cu:231-274,
+// the reference does in Python, QKNormRopeStoreCuda for the fused q/k norm +
+// rotary embedding + KV write and SampleTokensCuda for the sampler.  Each
+// function validates like the reference's TORCH_CHECKs (csrc/paged_attention/paged_attention_gemv.cu:231-274,
 // paged_attention_gemm.cu:314-358), allocates the output (and the split-KV
 // workspace) with the caching allocator, and calls the C ABI on the current
 // CUDA stream.  The same functions are also registered as torch.ops.femtovllm_b200.*.
@@ -256,6 +256,64 @@ torch::Tensor BuildSlotMappingCuda(torch::Tensor positions, std::optional<torch:
   return slots;
 }
 
+// Next-token ids (int64, (B,)) from logits (B, vocab): the reference's Sampler.forward
+// (femtovllm/engine/sampler.py:15-114) with device tensors in place of its Python lists.
+// rng_state: int64 (2,) {seed, offset} on the device, advanced by one per call.  workspace:
+// optional uint8 buffer of fvb_sample_workspace_size bytes, zero before its first use
+// (kept zero by every call); a fresh zeroed one is allocated when absent.
+torch::Tensor SampleTokensCuda(torch::Tensor logits, torch::Tensor temperatures,
+                               c10::optional<torch::Tensor> presence_penalties,
+                               c10::optional<torch::Tensor> token_table, torch::Tensor rng_state,
+                               c10::optional<torch::Tensor> workspace) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1,
+              "logits must be a (B, vocab) CUDA tensor with contiguous rows");
+  const int64_t B = logits.size(0), V = logits.size(1);
+  TORCH_CHECK(temperatures.is_cuda() && temperatures.scalar_type() == torch::kFloat32 &&
+                  temperatures.is_contiguous() && temperatures.numel() == B,
+              "temperatures must be a contiguous float32 CUDA tensor of B entries");
+  const float* pens = nullptr;
+  if (presence_penalties.has_value()) {
+    TORCH_CHECK(presence_penalties->is_cuda() && presence_penalties->scalar_type() == torch::kFloat32 &&
+                    presence_penalties->is_contiguous() && presence_penalties->numel() == B,
+                "presence_penalties must be a contiguous float32 CUDA tensor of B entries");
+    pens = presence_penalties->data_ptr<float>();
+  }
+  const int64_t* table = nullptr;
+  int64_t table_stride = 0, table_len = 0;
+  if (token_table.has_value() && token_table->numel() > 0) {
+    TORCH_CHECK(token_table->is_cuda() && token_table->scalar_type() == torch::kInt64 && token_table->dim() == 2 &&
+                    token_table->size(0) == B && token_table->stride(1) == 1,
+                "token_table must be an int64 (B, table_len) CUDA tensor with contiguous rows");
+    table = token_table->data_ptr<int64_t>();
+    table_stride = token_table->stride(0);
+    table_len = token_table->size(1);
+  }
+  TORCH_CHECK(rng_state.is_cuda() && rng_state.scalar_type() == torch::kInt64 && rng_state.numel() == 2 &&
+                  rng_state.is_contiguous(),
+              "rng_state must be a contiguous int64 CUDA tensor {seed, offset}");
+  c10::cuda::CUDAGuard guard(logits.device());
+  const size_t ws_bytes = fvb_sample_workspace_size(int(B), V);
+  torch::Tensor ws;
+  if (workspace.has_value()) {
+    ws = *workspace;
+    TORCH_CHECK(ws.is_cuda() && ws.is_contiguous() && size_t(ws.nbytes()) >= ws_bytes,
+                "workspace must be a contiguous CUDA buffer of at least ", ws_bytes, " bytes");
+  } else {
+    ws = torch::zeros({int64_t(ws_bytes > 0 ? ws_bytes : 1)}, logits.options().dtype(torch::kUInt8));
+  }
+  auto out = torch::empty({B}, logits.options().dtype(torch::kInt64));
+  check_status(fvb_sample_tokens(logits.data_ptr(), logits.stride(0), int(B), V, dtype_code(logits.scalar_type()),
+                                 temperatures.data_ptr<float>(), pens, table, table_stride, table_len,
+                                 reinterpret_cast<uint64_t*>(rng_state.data_ptr<int64_t>()), out.data_ptr<int64_t>(),
+                                 ws.data_ptr(), size_t(ws.nbytes()), stream_of(logits)),
+               "SampleTokensCuda");
+  return out;
+}
+
+int64_t SampleWorkspaceSize(int64_t num_rows, int64_t vocab) {
+  return int64_t(fvb_sample_workspace_size(int(num_rows), vocab));
+}
+
 std::tuple<int64_t, int64_t> ReadDeviceError() {
   int code = 0, info = 0;
   check_status(fvb_read_device_error(&code, &info,
@@ -281,6 +339,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "positions, cu_seqlens, kv_lens, padded block tables and slot mapping from per-sequence counts");
   m.def("QKNormRopeStoreCuda", &QKNormRopeStoreCuda,
         "fused q/k RMSNorm + rotary embedding + KV-cache write; returns q as (n_heads, num_tokens, d_head)");
+  m.def("SampleTokensCuda", &SampleTokensCuda,
+        "next-token ids: presence penalty, greedy argmax / temperature sampling (one launch)", py::arg("logits"),
+        py::arg("temperatures"), py::arg("presence_penalties") = py::none(), py::arg("token_table") = py::none(),
+        py::arg("rng_state"), py::arg("workspace") = py::none());
+  m.def("SampleWorkspaceSize", &SampleWorkspaceSize, "workspace bytes of SampleTokensCuda");
   m.def("ReadDeviceError", &ReadDeviceError, "read and clear the device error word (synchronizes)");
 }
 
@@ -300,6 +363,9 @@ TORCH_LIBRARY(femtovllm_b200, m) {
   m.def(
       "build_varlen_metadata(Tensor num_computed, Tensor num_new, Tensor flat_blocks, Tensor cu_blocks, "
       "int max_blocks_per_seq, int num_tokens) -> Tensor[]");
+  m.def(
+      "sample_tokens(Tensor logits, Tensor temperatures, Tensor? presence_penalties, Tensor? token_table, "
+      "Tensor(a!) rng_state, Tensor(b!)? workspace) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
@@ -309,4 +375,5 @@ TORCH_LIBRARY_IMPL(femtovllm_b200, CUDA, m) {
   m.impl("build_slot_mapping", &BuildSlotMappingCuda);
   m.impl("qk_norm_rope_store", &QKNormRopeStoreCuda);
   m.impl("build_varlen_metadata", &BuildVarlenMetadataCuda);
+  m.impl("sample_tokens", &SampleTokensCuda);
 }

@@ -53,6 +53,7 @@ CU_SOURCES = [
     "store_kvcache.cu",
     "qk_norm_rope.cu",
     "metadata.cu",
+    "sampler.cu",
     "decode.cu",
     "decode_noalloc.cu",
     "prefill_simt.cu",

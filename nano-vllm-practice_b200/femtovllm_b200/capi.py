@@ -60,6 +60,12 @@ _SIGNATURES = {
          c_float, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p,
          c_void_p, c_int64, c_int, c_int, c_void_p],
     ),
+    "fvb_sample_workspace_size": (c_size_t, [c_int, c_int64]),
+    "fvb_sample_tokens": (
+        c_int,
+        [c_void_p, c_int64, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+         c_void_p, c_void_p, c_size_t, c_void_p],
+    ),
     "fvb_paged_attention_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "fvb_paged_attention_decode": (
         c_int,

@@ -13,7 +13,9 @@ plus ``store_kvcache``, the slot-mapped KV write that replaces the Python
 loops of ``femtovllm/models/qwen/qwen3.py:240-264, 322-366``,
 ``build_slot_mapping``, which computes its ``slot_mapping`` on the device, and
 ``qk_norm_rope_store``, which fuses the q/k RMSNorm and rotary embedding of
-``qwen3.py:234-238`` with that write and hands q back head-major.
+``qwen3.py:234-238`` with that write and hands q back head-major, and
+``sample_tokens``, the arithmetic of ``femtovllm/engine/sampler.py`` in one
+launch (the drop-in ``Sampler`` module is ``femtovllm_b200.sampler``).
 
 The reference routes each op through a Triton/CUDA backend switch
 (``femtovllm._DEV``, ``ImplCustomKernel``).  That router is gone: ``impl`` is
@@ -232,6 +234,56 @@ def qk_norm_rope_store(
         q, k, v, q_norm_weight.contiguous(), k_norm_weight.contiguous(), float(eps), rope_cos.contiguous(),
         rope_sin.contiguous(), positions.contiguous(), k_pool, v_pool, slot_mapping.contiguous()
     )
+
+
+def new_rng_state(seed: int | None = None, device: torch.device | str = "cuda") -> torch.Tensor:
+    """Device RNG state ``{seed, offset}`` (int64, 2) for :func:`sample_tokens`; a seed drawn from
+    torch's global CPU generator when none is given (so ``torch.manual_seed`` makes runs repeat)."""
+    if seed is None:
+        seed = int(torch.randint(0, 2**62, (1,)).item())
+    return torch.tensor([seed, 0], dtype=torch.int64, device=device)
+
+
+def sample_workspace(num_rows: int, vocab: int, device: torch.device | str = "cuda") -> torch.Tensor:
+    """Zeroed workspace for :func:`sample_tokens`, reusable across calls (each call leaves it zero)."""
+    return torch.zeros(max(int(_cuda_backend.SampleWorkspaceSize(num_rows, vocab)), 1), dtype=torch.uint8,
+                       device=device)
+
+
+def sample_tokens(
+    logits: torch.Tensor,
+    temperatures: torch.Tensor,
+    presence_penalties: torch.Tensor | None = None,
+    token_table: torch.Tensor | None = None,
+    rng_state: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Next-token ids ``(B,)`` int64 from ``logits`` ``(B, vocab)``, on the device, in one launch.
+
+    The arithmetic of the reference's ``Sampler.forward`` (``femtovllm/engine/sampler.py:15-114``):
+    when any ``|presence_penalties| > 1e-5``, every token that occurs in a row of ``token_table``
+    (``(B, L)`` int64; entries outside ``[0, vocab)`` are padding, as the reference's pad id
+    ``vocab``) loses that row's penalty; rows with ``temperatures < 1e-5`` take the first argmax,
+    the others one draw from ``softmax(logits / T)``.  ``rng_state`` (:func:`new_rng_state`) is
+    advanced on the device by every call, so the op can be captured in a CUDA graph together
+    with a persistent ``workspace`` (:func:`sample_workspace`).
+    """
+    if not logits.is_cuda:
+        raise ValueError(f"Argument 'logits' must be a CUDA tensor. Got device={logits.device}")
+    dev = logits.device
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    temperatures = temperatures.to(device=dev, dtype=torch.float32).contiguous()
+    if presence_penalties is not None:
+        presence_penalties = presence_penalties.to(device=dev, dtype=torch.float32).contiguous()
+    if token_table is not None:
+        token_table = token_table.to(device=dev, dtype=torch.int64)
+        if token_table.stride(-1) != 1:
+            token_table = token_table.contiguous()
+    if rng_state is None:
+        rng_state = new_rng_state(device=dev)
+    return _cuda_backend.SampleTokensCuda(logits, temperatures, presence_penalties, token_table, rng_state,
+                                          workspace)
 
 
 def read_device_error() -> tuple[int, int]:

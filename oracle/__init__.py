@@ -11,7 +11,9 @@ parts of the attention hot path:
 * the stage before them: q/k RMSNorm, rotary embedding and the KV write
   (``oracle/qk_norm_rope.py``),
 * the per-step metadata (positions, cu_seqlens, kv_lens, padded block tables)
-  the engine builds for them (``oracle/metadata.py``).
+  the engine builds for them (``oracle/metadata.py``),
+* the next-token sampler that consumes the step's logits: presence penalty,
+  greedy argmax, temperature sampling (``oracle/sampler.py``).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 ``--impl reference`` legs of ``bench.py`` may import it, and only as the
@@ -23,7 +25,8 @@ own ``QwenSelfAttention.forward_varlen_pytorch`` and its KV-write loops
 (``femtovllm/models/qwen/qwen3.py:240-264, 322-366, 389-544``) on CPU, by
 ``tests/golden/make_golden.py``; the ``norm_rope_*`` fixtures record the
 reference's q_norm / k_norm / QwenRotaryEmbedding and write loop
-(``qwen3.py:17-138, 181-183, 228-264, 308-366``).  ``tests/test_oracle_golden.py``
+(``qwen3.py:17-138, 181-183, 228-264, 308-366``); ``sampler.npz`` records the
+reference's ``Sampler`` (``femtovllm/engine/sampler.py``).  ``tests/test_oracle_golden.py``
 checks this package against every one of those fixtures.
 """
 
@@ -43,3 +46,4 @@ from oracle.qk_norm_rope import (  # noqa: F401
     rope_tables,
 )
 from oracle.metadata import varlen_metadata  # noqa: F401,E402
+from oracle import sampler  # noqa: F401,E402

@@ -85,3 +85,23 @@ def qk_norm_rope_store(q, k, v, q_w, k_w, eps, cos, sin, positions, k_pool, v_po
     st = qk_norm_rope_store_status(q, k, v, q_w, k_w, eps, cos, sin, positions, k_pool, v_pool, slot_mapping, q_out)
     capi.check(st, "fvb_qk_norm_rope_store")
     return q_out
+
+
+def sample_tokens(logits, temperatures, presence_penalties, token_table, rng_state, workspace=None):
+    """fvb_sample_tokens on a (B, vocab) logits view with contiguous rows; returns int64 ids (B,)."""
+    B, V = logits.shape
+    assert logits.stride(1) == 1
+    out = torch.empty(B, dtype=torch.int64, device=logits.device)
+    ws_bytes = lib().fvb_sample_workspace_size(B, V)
+    if workspace is None:
+        workspace = torch.zeros(max(ws_bytes, 1), dtype=torch.uint8, device=logits.device)
+    has_table = token_table is not None and token_table.numel() > 0
+    st = lib().fvb_sample_tokens(
+        logits.data_ptr(), logits.stride(0), B, V, capi.dtype_code(logits.dtype), temperatures.data_ptr(),
+        presence_penalties.data_ptr() if presence_penalties is not None else None,
+        token_table.data_ptr() if has_table else None, token_table.stride(0) if has_table else 0,
+        token_table.shape[1] if has_table else 0, rng_state.data_ptr(), out.data_ptr(), workspace.data_ptr(),
+        workspace.numel(), _stream(),
+    )
+    capi.check(st, "fvb_sample_tokens")
+    return out

@@ -46,7 +46,9 @@ def golden_after(d: dict, which: str) -> np.ndarray:
     return pool
 
 
-GOLDEN_CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("norm_rope_", "metadata_")))
+GOLDEN_CASES = sorted(
+    p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("norm_rope_", "metadata_", "sampler"))
+)
 NORM_ROPE_CASES = sorted(p.stem for p in GOLDEN.glob("norm_rope_*.npz"))
 
 
@@ -73,3 +75,19 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+def load_sampler_cases() -> dict:
+    """tests/golden/sampler.npz as {case: {dtype, logits, temps, pens, table, counts}}."""
+    z = np.load(GOLDEN / "sampler.npz")
+    out = {}
+    for name in (str(n) for n in z["names"]):
+        out[name] = {k: z[f"{name}_{k}"] for k in ("logits", "temps", "pens", "table", "counts")}
+        out[name]["dtype"] = str(z[f"{name}_dtype"])
+    return out
+
+
+def chi2_critical(dof: int, alpha: float = 1e-4) -> float:
+    from scipy.stats import chi2
+
+    return float(chi2.ppf(1.0 - alpha, dof))

@@ -31,6 +31,10 @@ fuses.
 ``ModelRunner._route_prefill`` / ``_route_decode`` (``model_runner.py:159-339``)
 build from scheduled sequences, for ``build_varlen_metadata``.
 
+``sampler.npz`` records the reference's ``Sampler`` (``femtovllm/engine/sampler.py``)
+run on stand-in sequences: the ids of greedy rows and the token counts of many draws
+of sampled rows, for ``sample_tokens``.
+
 All inputs are bf16-representable (stored as bf16 bits) so one fixture serves
 both the fp32 and the bf16 checks; the reference runs in fp32.  Each fixture
 stores the pools before the write and only the rows the reference changed.
@@ -376,6 +380,66 @@ def run_reference_routes(ref: Path):
     print("metadata_routes: prefill T=%d, decode B=%d" % (int(num_new.sum()), len(dec_computed)))
 
 
+def sampler_cases():
+    """Logit batches for the reference Sampler: greedy rows (exact ids: ties, penalties that move
+    the argmax, negative and tiny penalties) and sampled rows over a small vocabulary (counts of
+    many draws, with and without the batch-wide penalty that switches bf16 logits to fp32)."""
+    g = torch.Generator().manual_seed(77)
+    V = 1000
+    out = []
+    lg = (torch.randn(6, V, generator=g) * 3).to(torch.bfloat16)
+    lg[0, 10] = lg[0, 500] = lg[0].max() + 1  # a tie: the first index wins
+    out.append(dict(name="greedy_bf16", logits=lg, temps=[0.0] * 6, pens=[0.0] * 6, tables=[[]] * 6, draws=1))
+    lg = torch.randn(6, V, generator=g) * 2
+    top = lg.argmax(dim=1).tolist()
+    tables = [[top[0], 3, 3, 999], [], [top[2], top[2]], [7, 8, 9], [top[4], 0], [top[5]]]
+    lg[3, 8] = lg[3].max() - 0.1  # a negative penalty lifts token 8 over the maximum
+    out.append(dict(name="greedy_pen_f32", logits=lg, temps=[0.0] * 6, pens=[1.0, 0.0, 0.5, -0.3, 2.0, 1e-6],
+                    tables=tables, draws=1))
+    Vs = 12
+    base = torch.tensor([2.9, 2.1, 1.3, 0.2, -0.7, 3.3, 1.0, -2.0, 0.55, 2.6, -1.1, 1.9])
+    lg = torch.stack([base, base.flip(0), base * 1.7, base - 1.0]).to(torch.bfloat16)
+    out.append(dict(name="dist_bf16", logits=lg, temps=[0.7, 1.0, 1.5, 0.3], pens=[0.0] * 4, tables=[[]] * 4,
+                    draws=20000))
+    out.append(dict(name="dist_pen", logits=lg.clone(), temps=[0.7, 1.0, 1.5, 0.0], pens=[1.0, 0.0, 0.5, 0.0],
+                    tables=[[0, 5, Vs, Vs], [1, 2], [5, 9, 0], [3]], draws=20000))
+    return out
+
+
+def run_reference_sampler(ref: Path):
+    """The reference's Sampler.forward (femtovllm/engine/sampler.py:15-114) on CPU with stand-in
+    sequences: greedy ids of every row and, over `draws` calls, the count of each sampled token."""
+    from femtovllm.engine.sampler import Sampler
+
+    torch.manual_seed(5)
+    sampler = Sampler()
+    out = {}
+    for case in sampler_cases():
+        lg = case["logits"]
+        B, V = lg.shape
+        seqs = [(types.SimpleNamespace(token_ids=list(t), sampling_params=types.SimpleNamespace(
+            temperature=float(tp), presence_penalty=float(pp))), 1)
+            for t, tp, pp in zip(case["tables"], case["temps"], case["pens"])]
+        counts = np.zeros((B, V), np.int64)
+        for _ in range(case["draws"]):
+            ids = sampler(lg.clone(), seqs)
+            counts[np.arange(B), ids] += 1
+        width = max(1, max(len(t) for t in case["tables"]))
+        table = np.full((B, width), V, np.int64)
+        for i, t in enumerate(case["tables"]):
+            table[i, : len(t)] = t
+        n = case["name"]
+        out[f"{n}_dtype"] = np.array("bf16" if lg.dtype == torch.bfloat16 else "f32")
+        out[f"{n}_logits"] = lg.float().numpy()
+        out[f"{n}_temps"] = np.asarray(case["temps"], np.float32)
+        out[f"{n}_pens"] = np.asarray(case["pens"], np.float32)
+        out[f"{n}_table"] = table
+        out[f"{n}_counts"] = counts
+        print(f"sampler {n}: B={B} V={V} draws={case['draws']}")
+    out["names"] = np.array([c["name"] for c in sampler_cases()])
+    np.savez_compressed(HERE / "sampler.npz", **out)
+
+
 def _bits(t: torch.Tensor) -> np.ndarray:
     return t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
 
@@ -389,9 +453,13 @@ def _changed_rows(before, after):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--which", choices=["attention", "norm_rope", "metadata", "all"], default="all")
+    ap.add_argument("--which", choices=["attention", "norm_rope", "metadata", "sampler", "all"], default="all")
     args = ap.parse_args()
     femtovllm, QSA, VAM = _import_reference(args.reference)
+    if args.which in ("sampler", "all"):
+        run_reference_sampler(args.reference)
+        if args.which == "sampler":
+            return
     if args.which in ("metadata", "all"):
         run_reference_routes(args.reference)
         if args.which == "metadata":

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import GOLDEN_CASES, golden_after, load_golden
+from conftest import GOLDEN_CASES, chi2_critical, golden_after, load_golden, load_sampler_cases
 
 
 @pytest.mark.parametrize("name", GOLDEN_CASES)
@@ -141,3 +141,65 @@ def test_varlen_metadata_matches_reference_routes(route):
     assert md["max_q_len"] == int(z[f"{route}_max_q_len"]) and md["max_kv_len"] == int(z[f"{route}_max_kv_len"])
     if f"{route}_cu_seqlens" in z.files:
         assert np.array_equal(md["cu_seqlens"], z[f"{route}_cu_seqlens"])
+
+
+# ---------------------------------------------------------------------------
+# Sampler (femtovllm/engine/sampler.py)
+# ---------------------------------------------------------------------------
+def test_philox_known_answers():
+    """Philox4x32-10 known-answer vectors of its authors' Random123 distribution."""
+    from oracle.sampler import philox4x32_10
+
+    kat = [
+        ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+        ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+        ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+         (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+    ]
+    for ctr, key, want in kat:
+        got = philox4x32_10(np.array([ctr], np.uint64), key)[0]
+        assert tuple(int(x) for x in got) == want
+
+
+def test_sampler_greedy_matches_reference():
+    """Greedy rows: the reference's ids (ties, penalties that move the argmax, negative and tiny penalties)."""
+    from oracle import sampler as S
+
+    cases = load_sampler_cases()
+    for name, c in cases.items():
+        greedy = c["temps"] < 1e-5
+        if not greedy.any():
+            continue
+        ref_ids = c["counts"].argmax(axis=1)
+        assert (c["counts"][greedy].max(axis=1) == c["counts"][greedy].sum(axis=1)).all(), name
+        ids, _ = S.sample(c["logits"], c["dtype"], c["temps"], c["pens"], c["table"])
+        np.testing.assert_array_equal(ids[greedy], ref_ids[greedy], err_msg=name)
+
+
+def test_sampler_distribution_matches_reference_draws():
+    """Sampled rows: the reference's multinomial counts fit the oracle's probabilities (chi-square,
+    alpha 1e-4), with and without the batch-wide penalty that keeps bf16 logits in fp32."""
+    from oracle import sampler as S
+
+    for name, c in load_sampler_cases().items():
+        p = S.probabilities(c["logits"], c["dtype"], c["temps"], c["pens"], c["table"])
+        for b in np.nonzero(c["temps"] >= 1e-5)[0]:
+            n = c["counts"][b].sum()
+            e = p[b] * n
+            m = e > 0
+            assert c["counts"][b][~m].sum() == 0, (name, b)
+            chi = float((((c["counts"][b] - e) ** 2)[m] / e[m]).sum())
+            assert chi < chi2_critical(int(m.sum()) - 1), (name, b, chi)
+
+
+def test_sampler_oracle_catches_a_planted_temperature_error():
+    """The distribution test has power: dividing by T twice fails it."""
+    from oracle import sampler as S
+
+    c = load_sampler_cases()["dist_bf16"]
+    bad_t = c["temps"] * c["temps"]
+    p = S.probabilities(c["logits"], c["dtype"], bad_t, c["pens"], c["table"])
+    b = 0
+    e = p[b] * c["counts"][b].sum()
+    chi = float((((c["counts"][b] - e) ** 2) / e).sum())
+    assert chi > chi2_critical(len(e) - 1)
