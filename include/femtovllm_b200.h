@@ -97,8 +97,8 @@ FVB_API int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride
                       void* stream);
 
 /*
- * Next-token sampling over num_rows logit rows in one launch: the reference's Sampler.forward
- * (femtovllm/engine/sampler.py:15-114), which the model runner calls on lm_head's output
+ * Next-token sampling over num_rows logit rows (two kernel launches, one pass over the logits): the
+ * reference's Sampler.forward (femtovllm/engine/sampler.py:15-114), which the model runner calls on lm_head's output
  * (femtovllm/engine/model_runner.py:150-157).  Row b: logits[b * row_stride + i], i < vocab.
  *   apply = any |presence_penalties[r]| > 1e-5 over all rows (sampler.py:31-35);
  *   x[i] = logits[b][i] - presence_penalties[b] if apply and token i occurs in
@@ -111,8 +111,9 @@ FVB_API int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride
  *          reference's in-place division of 16-bit logits does.
  * presence_penalties may be NULL (no penalty); token_table int64 [num_rows][table_stride].
  * rng_state: device uint64[2] {seed, offset}; each launch adds 1 to offset, on the device.
- * workspace: fvb_sample_workspace_size(num_rows, vocab) bytes, 16-byte aligned; its counters must be
- * zero before the first launch (e.g. cudaMemsetAsync once) and every launch leaves them zero.
+ * workspace: fvb_sample_workspace_size(num_rows, vocab) bytes, 16-byte aligned; its first 4 bytes (a
+ * counter) must be zero before the first launch (e.g. cudaMemsetAsync once) and every launch leaves them
+ * zero.
  * Replaces the reference's Python lists, count matrix and per-group launches; no counterpart in its
  * native module.
  */

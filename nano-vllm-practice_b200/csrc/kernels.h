@@ -137,7 +137,7 @@ cudaError_t launch_build_varlen_metadata(const int32_t* num_computed, const int3
                                          int64_t* slot_mapping, int* err, cudaStream_t stream);
 
 // Next-token sampling (sampler.cu): presence penalty, greedy argmax, temperature
-// sampling; workspace counters zero before the first launch and left zero after each.
+// sampling (two launches); the workspace counter is zero before the first launch and left zero.
 size_t sample_workspace_size(int num_rows, int64_t vocab);
 cudaError_t launch_sample(const void* logits, int64_t row_stride, int num_rows, int64_t vocab, int dtype,
                           const float* temps, const float* pens, const int64_t* table, int64_t table_stride,

@@ -16,14 +16,14 @@
 //     softmax(x / T) (:106-109) by inverse CDF in vocabulary order with one
 //     Philox4x32-10 uniform per row.
 //
-// Grid: one CTA per (row, chunk of the vocabulary); each of its 8 warps reduces
-// a contiguous sub-chunk to a partial, (max, first index) for greedy rows or
-// (max, sum of 2^(x2 - max)) in the log2 domain for sampled rows.  The last CTA
-// of a row (an atomic ticket) merges the partials, draws the uniform, finds the
-// sub-chunk holding it and rescans only that sub-chunk (at most 4096 logits,
-// from L2) for the exact token.  The last row to finish advances the RNG
-// offset, so a CUDA-graph replay draws fresh numbers.  Tickets are reset by
-// the kernel that used them.
+// Two launches.  sample_partials_kernel streams the logits once: one wave of CTAs, each owning
+// an equal span of the batch (one or more row parts); each of a CTA's 8 warps folds a
+// contiguous run of a part into a partial, (max, first index) for greedy rows or (m, s) with
+// s = sum 2^(x2 - m) in the log2 domain for sampled rows.  No CTA-wide barrier on that path
+// (only around the presence bitmap of penalised rows).  sample_finish_kernel, one CTA per
+// row, merges the row's partials, draws the Philox uniform, finds the run holding it and
+// rescans only that run (from L2) for the exact token; the last CTA to finish advances the
+// RNG offset, so a CUDA-graph replay draws fresh numbers.
 #include <algorithm>
 
 #include "common.cuh"
@@ -34,8 +34,8 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kMinChunk = 2048;   // multiple of 32 * kWarps, so every sub-chunk is 16-byte aligned
-constexpr int kMaxChunk = 32768;  // presence bitmap of one chunk: kMaxChunk / 32 words of shared memory
+constexpr int kMinPart = 2048;     // columns of the smallest CTA span
+constexpr int kMaxPart = 131072;   // presence bitmap of one part: kMaxPart / 32 words of shared memory
 constexpr float kGreedyBelow = 1e-5f;
 constexpr float kPenaltyAbove = 1e-5f;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -68,9 +68,12 @@ struct SampleArgs {
   int64_t table_stride, table_len;
   unsigned long long* rng;  // {seed, offset}
   int64_t* out;
-  float2* partials;   // [row][split][warp]
-  unsigned* tickets;  // [num_rows] per-row tickets, then the grid ticket
-  int chunk, nsplit;
+  float2* partials;   // [row][part slot < maxparts][warp][sub-run < maxsub]
+  uint32_t* presence; // [row][vocab / 32]: presence bitmaps of penalised rows, for the finish kernel
+  unsigned* ctl;      // {grid ticket, batch-wide penalty flag}
+  int64_t vp, per;    // row length rounded up to 256; columns per CTA
+  int maxparts, maxsub;  // part slots per row; partials per warp run
+  int64_t pwords;        // presence words per row: ceil(vocab / 32)
   bool vec_ok;
 };
 
@@ -80,6 +83,7 @@ struct RowMode {
   int mode;
   bool pen_on;
   float pen, t, inv_t, c;  // c = log2(e) / T
+  float kpen;              // 2^(-pen * c) - 1: weight change of a penalised token (sampled rows)
 };
 
 template <typename T>
@@ -127,12 +131,6 @@ __device__ __forceinline__ int load_group(const T* row, int64_t i, int64_t hi, b
   return n;
 }
 
-// cp.async.bulk.prefetch.L2: the copy engine pulls [p, p + bytes) into L2 (16-byte aligned, size
-// a multiple of 16); a hint, nothing waits on it.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ uint32_t presence_bits(const uint32_t* bitmap, int64_t off, int ve) {
   return (bitmap[off >> 5] >> (off & 31)) & ((1u << ve) - 1u);
 }
@@ -158,76 +156,196 @@ __device__ __forceinline__ float rounded_quotient(float x, const RowMode& md) {
   return round_to<T>(r == r ? q1 : q);
 }
 
-// Folds NV groups of logits (group u starts at index i + u * step; entries past the range are
-// -inf) into a lane's partial: greedy (max, first index); sampled (m, s) meaning s * 2^m in the
-// log2 domain, s kept in four independent sums.  Sampled rows rescale lazily: the reference m
-// moves only when a group's maximum passes it by more than 8, so weights stay below 2^8.
-template <typename T, int MODE, bool PEN, int NV>
-__device__ __forceinline__ void consume(float* x, const uint32_t* bits, int64_t i, int step, const RowMode& md,
-                                        float& pa, float* acc, int& pi) {
-  constexpr int VE = 16 / sizeof(T), N = NV * VE;
-#pragma unroll
-  for (int j = 0; j < N; ++j) x[j] = penalize<PEN>(x[j], bits[j / VE], j % VE, md.pen);
-  if (MODE == kModeSampleRounded) {
-#pragma unroll
-    for (int j = 0; j < N; ++j) x[j] = rounded_quotient<T>(x[j], md);
+// Greedy partial merge: larger value wins, the smaller index on ties (torch.argmax
+// returns the first maximal index); index INT_MAX marks "nothing seen".
+__device__ __forceinline__ void merge_max(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
   }
-  const float g = tree_max<N>(x);
-  if (MODE == kModeGreedy) {
-    if (g > pa) {  // strictly: an earlier (smaller) index keeps a tie; -inf never wins
-      int k = N - 1;
+}
+
+// Sampled partial merge in the log2 domain: (m, s) stands for s * 2^m.
+__device__ __forceinline__ void merge_lse(float& m, float& s, float m2, float s2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = m2;
+    s = s2;
+    return;
+  }
+  if (m2 > m) {
+    s = s * fast_exp2(m - m2) + s2;
+    m = m2;
+  } else {
+    s += s2 * fast_exp2(m2 - m);
+  }
+}
+
+// Columns per partial: each warp reports one partial per 2048 columns of its run, so the finish
+// kernel rescans at most 2048 logits (one 16-byte vector a thread) to place the draw.
+constexpr int kSubCols = 2048;
+
+// A lane's running state over one sub-run.  Greedy: max and the first column holding it.  Sampled:
+// (m, s) meaning s * 2^m in the log2 domain, s in four independent sums plus `accp`, the part of s
+// from penalised tokens.
+struct Lane {
+  float pa, accp;
+  float acc[4];
+  int pbase;
+};
+
+__device__ __forceinline__ void lane_reset(Lane& st) {
+  st.pa = -INFINITY;
+  st.accp = 0.f;
+  st.acc[0] = st.acc[1] = st.acc[2] = st.acc[3] = 0.f;
+  st.pbase = -1;
+}
+
+// Folds one 16-byte vector (columns i..i+VE-1; entries past the range are -inf) into a lane.
+// Greedy rows penalise every element.  Sampled rows on the fp32 path weigh the raw logits and
+// sum the weights of penalised tokens apart: 2^((l - p) c - m) = 2^(l c - m) * 2^(-p c), so the
+// penalty becomes one factor at the end instead of work on every element.  Sampled rows rescale
+// lazily: m moves only when a vector's maximum passes it by more than 8 (weights stay below 2^8;
+// a negative penalty lifts penalised weights by 2^(|p| c) on top).  The row's treatment is a
+// warp-uniform branch.
+template <typename T>
+__device__ __forceinline__ void consume(float* x, uint32_t bits, int i, const RowMode& md, Lane& st) {
+  constexpr int VE = 16 / sizeof(T);
+  if (md.mode == kModeGreedy) {
+    if (md.pen_on) {
 #pragma unroll
-      for (int j = N - 1; j >= 0; --j)
-        if (x[j] == g) k = j;
-      pa = g;
-      pi = int(i + int64_t(k / VE) * step + k % VE);
+      for (int e = 0; e < VE; ++e) x[e] = penalize<true>(x[e], bits, e, md.pen);
+    }
+    const float g = tree_max<VE>(x);
+    if (g > st.pa) {  // strictly: an earlier vector keeps a tie; -inf never wins
+      int k = i + VE - 1;
+#pragma unroll
+      for (int e = VE - 2; e >= 0; --e)
+        if (x[e] == g) k = i + e;
+      st.pa = g;
+      st.pbase = k;  // the first column holding the new maximum
     }
     return;
   }
-  const float scale = MODE == kModeSampleF32 ? md.c : kLog2e;
-  const float gy = g * scale;
-  if (gy > pa + 8.f) {
-    const float f = ex2(pa - gy);  // 0 while pa is -inf
+  float scale = md.c;
+  if (md.mode == kModeSampleRounded) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc[q] *= f;
-    pa = gy;
+    for (int e = 0; e < VE; ++e) x[e] = rounded_quotient<T>(x[e], md);
+    scale = kLog2e;
   }
-  if (pa == -INFINITY) return;
+  const float gy = tree_max<VE>(x) * scale;  // scale > 0: the max commutes with it
+  if (gy > st.pa + 8.f) {
+    const float f = ex2(st.pa - gy);  // 0 while pa is -inf
 #pragma unroll
-  for (int j = 0; j < N; ++j) acc[j & 3] += ex2(fmaf(x[j], scale, -pa));
+    for (int q = 0; q < 4; ++q) st.acc[q] *= f;
+    st.accp *= f;
+    st.pa = gy;
+  }
+  if (st.pa == -INFINITY) return;
+#pragma unroll
+  for (int e = 0; e < VE; ++e) {
+    const float w = ex2(fmaf(x[e], scale, -st.pa));
+    st.acc[e & 3] += w;
+    if (bits & (1u << e)) st.accp += w;
+  }
 }
 
-// One warp's sub-chunk [lo, hi) of a row: U 16-byte loads in flight per lane while the
-// whole unrolled step is in range, then one group at a time with bounds.
-template <typename T, int MODE, bool PEN>
-__device__ __forceinline__ void pass1(const T* lrow, int64_t lo, int64_t hi, int64_t c0, bool vec_ok,
-                                      const uint32_t* bitmap, const RowMode& md, float& pa, float& pb, int& pi) {
-  constexpr int VE = 16 / sizeof(T), U = 4, STEP = 32 * VE;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int64_t i = lo + (threadIdx.x & 31) * VE;
-  if (vec_ok) {
-    for (; i + (U - 1) * STEP + VE <= hi; i += U * STEP) {
-      uint4 raw[U];
+// Reduces the warp's lanes to one partial and writes it (lane 0): greedy (value, first index);
+// sampled (m, s) with the penalty factor applied.
+__device__ __forceinline__ void emit(const Lane& st, const RowMode& md, float2* dst) {
+  const bool greedy = md.mode == kModeGreedy;
+  float pa = st.pa, pb = 0.f;
+  int pi = INT_MAX;
+  if (greedy) {
+    pi = st.pbase >= 0 ? st.pbase : INT_MAX;
+  } else {
+    pb = (st.acc[0] + st.acc[1]) + (st.acc[2] + st.acc[3]);
+    if (md.pen_on) pb = fmaxf(0.f, fmaf(md.kpen, st.accp, pb));
+  }
 #pragma unroll
-      for (int u = 0; u < U; ++u) raw[u] = ldg_nc_v4(lrow + i + u * STEP);
-      float x[U * VE];
-      uint32_t bits[U];
+  for (int o = 16; o > 0; o >>= 1) {
+    const float a2 = __shfl_xor_sync(0xffffffffu, pa, o);
+    const float b2 = __shfl_xor_sync(0xffffffffu, pb, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, pi, o);
+    if (greedy) merge_max(pa, pi, a2, i2);
+    else merge_lse(pa, pb, a2, b2);
+  }
+  if ((threadIdx.x & 31) == 0) *dst = make_float2(pa, greedy ? __int_as_float(pi) : pb);
+}
+
+// One warp's run [lo, hi) of a row, one partial per kSubCols columns (maxsub partials written,
+// empty ones neutral).  Warp-uniform loop, software-pipelined: while a lane folds its U current
+// 16-byte vectors the next U are in flight.  Column indices are 32-bit (vocab < 2^31).  Not with
+// 16-byte vectors when the row is not 16-byte aligned (vec_ok false): every load goes through the
+// bounded scalar path.
+template <typename T>
+__device__ __forceinline__ void pass1(const T* lrow, int lo, int hi, int c0, bool vec_ok, const uint32_t* bitmap,
+                                      const RowMode& md, float2* dst, int maxsub) {
+  constexpr int VE = 16 / sizeof(T), U = 2, STEP = 32 * VE, IT = U * STEP;
+  static_assert(kSubCols % IT == 0, "sub-runs are whole iterations");
+  const int lane = threadIdx.x & 31;
+  Lane st;
+  lane_reset(st);
+  int sub = 0, emitted = lo;  // partials written; columns covered by them end at `emitted`
+  int ib = lo;  // warp-uniform column of the current iteration
+  if (vec_ok && ib + IT <= hi) {
+    uint4 cur[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) cur[u] = ldg_nc_v4(lrow + ib + u * STEP + lane * VE);
+    while (true) {
+      const int nb = ib + IT;
+      const bool more = nb + IT <= hi;
+      uint4 nxt[U];
+      if (more) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) nxt[u] = ldg_nc_v4(lrow + nb + u * STEP + lane * VE);
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        unpack16<T>(raw[u], x + u * VE);
-        bits[u] = PEN ? presence_bits(bitmap, i + u * STEP - c0, VE) : 0u;
+        const int i = ib + u * STEP + lane * VE;
+        float x[VE];
+        unpack16<T>(cur[u], x);
+        const uint32_t bits = md.pen_on ? presence_bits(bitmap, i - c0, VE) : 0u;
+        consume<T>(x, bits, i, md, st);
       }
-      consume<T, MODE, PEN, U>(x, bits, i, STEP, md, pa, acc, pi);
+      ib = nb;
+      if ((ib - lo) % kSubCols == 0) {
+        emit(st, md, dst + sub);
+        ++sub;
+        emitted = ib;
+        lane_reset(st);
+      }
+      if (!more) break;
+#pragma unroll
+      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
     }
   }
-  for (; i < hi; i += STEP) {
+  // The rest, one vector per lane at a time with bounds.
+  for (; ib < hi; ib += STEP) {
+    if (ib > emitted && (ib - lo) % kSubCols == 0 && sub < maxsub) {
+      emit(st, md, dst + sub);
+      ++sub;
+      emitted = ib;
+      lane_reset(st);
+    }
+    const int i = ib + lane * VE;
     float x[VE];
-    uint32_t bits[1];
-    load_group<T>(lrow, i, hi, vec_ok, x);
-    bits[0] = PEN ? presence_bits(bitmap, i - c0, VE) : 0u;
-    consume<T, MODE, PEN, 1>(x, bits, i, STEP, md, pa, acc, pi);
+    if (i < hi) {
+      load_group<T>(lrow, i, hi, vec_ok, x);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VE; ++e) x[e] = -INFINITY;
+    }
+    const uint32_t bits = md.pen_on && i < hi ? presence_bits(bitmap, i - c0, VE) : 0u;
+    consume<T>(x, bits, i, md, st);
   }
-  pb = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  if (hi > emitted && sub < maxsub) {  // the last, partial sub-run
+    emit(st, md, dst + sub);
+    ++sub;
+  }
+  if (lane == 0)
+    for (; sub < maxsub; ++sub) dst[sub] = md.mode == kModeGreedy ? make_float2(-INFINITY, __int_as_float(INT_MAX))
+                                                                  : make_float2(-INFINITY, 0.f);
 }
 
 // Marks in `bitmap` the tokens of row `row`'s table that fall in [lo, lo + len): the table
@@ -262,31 +380,6 @@ __device__ void build_bitmap(const SampleArgs& a, int row, int64_t lo, int64_t l
     }
   }
   __syncthreads();
-}
-
-// Greedy partial merge: larger value wins, the smaller index on ties (torch.argmax
-// returns the first maximal index); index INT_MAX marks "nothing seen".
-__device__ __forceinline__ void merge_max(float& v, int& i, float v2, int i2) {
-  if (v2 > v || (v2 == v && i2 < i)) {
-    v = v2;
-    i = i2;
-  }
-}
-
-// Sampled partial merge in the log2 domain: (m, s) stands for s * 2^m.
-__device__ __forceinline__ void merge_lse(float& m, float& s, float m2, float s2) {
-  if (m2 == -INFINITY) return;
-  if (m == -INFINITY) {
-    m = m2;
-    s = s2;
-    return;
-  }
-  if (m2 > m) {
-    s = s * fast_exp2(m - m2) + s2;
-    m = m2;
-  } else {
-    s += s2 * fast_exp2(m2 - m);
-  }
 }
 
 // Exclusive block scan of one double per thread; returns the exclusive prefix, *total the sum.
@@ -330,93 +423,119 @@ __device__ int block_claimer(bool has_weight, double before, double target, int*
   return c;
 }
 
+// ---------------------------------------------------------------------------
+// Launch geometry.  The batch is laid out as rows of vp = vocab rounded up to 256 entries (the
+// padding is never read) and CTA c owns the span [c * per, (c + 1) * per) of that layout: one
+// or more row parts of equal total length, so the CTAs of the single wave finish together.  A
+// row's parts are numbered by slot (vocabulary order); each part's 8 warps take equal runs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t first_cta(int64_t r, const SampleArgs& a) { return r * a.vp / a.per; }
+__device__ __forceinline__ int parts_of_row(int64_t r, const SampleArgs& a) {
+  return int((r * a.vp + a.vp - 1) / a.per - first_cta(r, a) + 1);
+}
+// Columns [lo, hi) of part `slot` of row r, hi capped at the vocabulary (empty for padding).
+__device__ __forceinline__ void part_cols(const SampleArgs& a, int64_t r, int slot, int64_t& lo, int64_t& hi) {
+  const int64_t c = first_cta(r, a) + slot, rs = r * a.vp;
+  lo = max(c * a.per, rs) - rs;
+  hi = max(lo, min(min((c + 1) * a.per, rs + a.vp) - rs, a.vocab));
+}
+// Warp w's run of a part: multiples of 32 columns, so 16-byte vectors stay aligned.
+__device__ __forceinline__ void warp_cols(int64_t lo, int64_t hi, int w, int64_t& wlo, int64_t& whi) {
+  const int64_t sub = (hi - lo + 32 * kWarps - 1) / (32 * kWarps) * 32;
+  wlo = min(lo + w * sub, hi);
+  whi = min(wlo + sub, hi);
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 4) sample_kernel(SampleArgs a) {
-  constexpr int VE = 16 / sizeof(T);
-  __shared__ uint32_t bitmap[kMaxChunk / 32];
-  __shared__ double warp_sums[kWarps];
-  __shared__ float red_f[kWarps];
-  __shared__ int red_i[kWarps];
-  __shared__ int s_flag;
-  __shared__ double s_target;
-  __shared__ unsigned long long s_rng[2];
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int row = int(blockIdx.x / unsigned(a.nsplit));
-  const int split = int(blockIdx.x - unsigned(row) * unsigned(a.nsplit));
-  const T* lrow = static_cast<const T*>(a.logits) + int64_t(row) * a.row_stride;
-  const int64_t c0 = int64_t(split) * a.chunk;
-  const int64_t c1 = c0 + a.chunk < a.vocab ? c0 + a.chunk : a.vocab;
-  const int sub = a.chunk / kWarps;
-  const int64_t lo = c0 + int64_t(warp) * sub;
-  const int64_t hi = lo + sub < c1 ? lo + sub : c1;
-  // Start the HBM stream first: each warp asks the copy engine to bring its sub-chunk into L2
-  // while the CTA reads its parameters and builds the presence bitmap.
-  if (a.vec_ok && lane == 0 && hi > lo) {
-    const uint32_t bytes = uint32_t((hi - lo) * int64_t(sizeof(T))) & ~15u;
-    if (bytes) bulk_prefetch_l2(lrow + lo, bytes);
-  }
-
-  // Batch-wide penalty switch, as the reference decides it from all rows' parameters.
-  int anyp = 0;
-  if (a.pens != nullptr)
-    for (int r = threadIdx.x; r < a.num_rows; r += kThreads) anyp |= fabsf(__ldg(a.pens + r)) > kPenaltyAbove;
-  anyp = __syncthreads_or(anyp);
-
+__device__ __forceinline__ RowMode row_mode(const SampleArgs& a, float t, float pen, int anyp) {
   RowMode md;
-  const float t = __ldg(a.temps + row);
   const bool greedy = t < kGreedyBelow;
-  md.pen = anyp ? __ldg(a.pens + row) : 0.f;
+  md.pen = anyp ? pen : 0.f;
   md.pen_on = anyp && md.pen != 0.f && a.table_len > 0;
   md.mode = greedy ? kModeGreedy
                    : (!anyp && Elem<T>::kDtype != FVB_DTYPE_F32 ? kModeSampleRounded : kModeSampleF32);
   md.t = greedy ? 1.f : t;
   md.inv_t = greedy ? 1.f : 1.f / t;
   md.c = md.inv_t * kLog2e;
+  md.kpen = md.pen_on && !greedy ? ex2(-md.pen * md.c) - 1.f : 0.f;
+  return md;
+}
 
-  if (md.pen_on) build_bitmap(a, row, c0, c1 - c0, bitmap);
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 4) sample_partials_kernel(SampleArgs a) {
+  __shared__ uint32_t bitmap[kMaxPart / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t total = int64_t(a.num_rows) * a.vp;
+  const int64_t f0 = int64_t(blockIdx.x) * a.per, f1 = min(f0 + a.per, total);
+  // Batch-wide penalty switch, as the reference decides it from all rows' parameters, and the
+  // parameters of this CTA's rows (at most kThreads of them cached) in the same round trip.
+  __shared__ float s_temp[kThreads], s_pen[kThreads];
+  const int64_t row0 = f0 / a.vp;
+  const int nrows = f1 > f0 ? int((f1 - 1) / a.vp - row0 + 1) : 0;
+  if (threadIdx.x < nrows) {
+    s_temp[threadIdx.x] = __ldg(a.temps + row0 + threadIdx.x);
+    s_pen[threadIdx.x] = a.pens != nullptr ? __ldg(a.pens + row0 + threadIdx.x) : 0.f;
+  }
+  int anyp = 0;
+  if (a.pens != nullptr)
+    for (int r = threadIdx.x; r < a.num_rows; r += kThreads) anyp |= fabsf(__ldg(a.pens + r)) > kPenaltyAbove;
+  anyp = __syncthreads_or(anyp);
+  if (blockIdx.x == 0 && threadIdx.x == 0) a.ctl[1] = unsigned(anyp);
+  for (int64_t f = f0; f < f1;) {
+    const int64_t row = f / a.vp, fe = min(f1, (row + 1) * a.vp);
+    const int64_t lo = f - row * a.vp, hi = max(lo, min(fe - row * a.vp, a.vocab));
+    const int slot = int(blockIdx.x - first_cta(row, a));
+    const int rr = int(row - row0);
+    const RowMode md = rr < kThreads ? row_mode<T>(a, s_temp[rr], s_pen[rr], anyp)
+                                     : row_mode<T>(a, __ldg(a.temps + row), a.pens ? __ldg(a.pens + row) : 0.f, anyp);
+    if (md.pen_on) {
+      __syncthreads();  // every warp is done with the previous part's bitmap
+      build_bitmap(a, int(row), lo, hi - lo, bitmap);
+    }
+    const T* lrow = static_cast<const T*>(a.logits) + row * a.row_stride;
+    int64_t wlo, whi;
+    warp_cols(lo, hi, warp, wlo, whi);
+    pass1<T>(lrow, int(wlo), int(whi), int(lo), a.vec_ok, bitmap, md,
+             a.partials + ((row * a.maxparts + slot) * kWarps + warp) * a.maxsub, a.maxsub);
+    if (md.pen_on) {  // this warp's run of the bitmap, for the finish kernel's rescan
+      uint32_t* dst = a.presence + row * a.pwords;
+      for (int64_t w = wlo / 32 + lane; w < (whi + 31) / 32; w += 32) dst[w] = bitmap[w - lo / 32];
+    }
+    f = fe;
+  }
+}
 
-  // ---- pass 1: this warp's sub-chunk to one partial ----
-  float pa = -INFINITY, pb = 0.f;  // greedy: (value, index bits); sampled: (m, s)
-  int pi = INT_MAX;
-  switch (md.mode * 2 + int(md.pen_on)) {
-    case 0: pass1<T, kModeGreedy, false>(lrow, lo, hi, c0, a.vec_ok, bitmap, md, pa, pb, pi); break;
-    case 1: pass1<T, kModeGreedy, true>(lrow, lo, hi, c0, a.vec_ok, bitmap, md, pa, pb, pi); break;
-    case 2: pass1<T, kModeSampleF32, false>(lrow, lo, hi, c0, a.vec_ok, bitmap, md, pa, pb, pi); break;
-    case 3: pass1<T, kModeSampleF32, true>(lrow, lo, hi, c0, a.vec_ok, bitmap, md, pa, pb, pi); break;
-    case 4: pass1<T, kModeSampleRounded, false>(lrow, lo, hi, c0, a.vec_ok, bitmap, md, pa, pb, pi); break;
-    default: pass1<T, kModeSampleRounded, true>(lrow, lo, hi, c0, a.vec_ok, bitmap, md, pa, pb, pi); break;
-  }
-  // Warp reduction (lanes hold increasing, interleaved indices: ties go to the smaller index).
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float a2 = __shfl_xor_sync(0xffffffffu, pa, o);
-    const float b2 = __shfl_xor_sync(0xffffffffu, pb, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, pi, o);
-    if (greedy) merge_max(pa, pi, a2, i2);
-    else merge_lse(pa, pb, a2, b2);
-  }
-  float2* rp = a.partials + (int64_t(row) * a.nsplit) * kWarps;
-  if (lane == 0) {
-    rp[split * kWarps + warp] = make_float2(pa, greedy ? __int_as_float(pi) : pb);
-    __threadfence();
-  }
-  __syncthreads();
+struct Shared {
+  double warp_sums[kWarps];
+  float red_f[kWarps];
+  int red_i[kWarps];
+  int flag;
+  double target, obefore;
+  unsigned long long rng[2];
+};
+
+// One CTA per row: merge the row's partials; greedy rows take the maximum, sampled rows draw.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
+  constexpr int VE = 16 / sizeof(T);
+  __shared__ uint32_t bitmap[kSubCols / 32];
+  __shared__ Shared sm;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int row = blockIdx.x;
+  const T* lrow = static_cast<const T*>(a.logits) + int64_t(row) * a.row_stride;
   if (threadIdx.x == 0) {
-    __threadfence();
-    s_flag = atomicAdd(a.tickets + row, 1u) == unsigned(a.nsplit - 1);
+    sm.rng[0] = __ldcg(a.rng);
+    sm.rng[1] = __ldcg(a.rng + 1);
   }
-  __syncthreads();
-  if (!s_flag) return;
-
-  // ---- the last CTA of the row: merge, draw, rescan ----
-  __threadfence();
-  if (threadIdx.x == 0) {
-    s_rng[0] = __ldcg(a.rng);
-    s_rng[1] = __ldcg(a.rng + 1);
-  }
-  const int np = a.nsplit * kWarps;
-  if (greedy) {
+  const float t_row = __ldg(a.temps + row), p_row = a.pens != nullptr ? __ldg(a.pens + row) : 0.f;
+  // Launched as a programmatic dependent of sample_partials_kernel: everything above overlaps its
+  // tail; from here on its partials, flag and presence words are complete and visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int anyp = int(__ldcg(a.ctl + 1));
+  const RowMode md = row_mode<T>(a, t_row, p_row, anyp);
+  const float2* rp = a.partials + int64_t(row) * a.maxparts * kWarps * a.maxsub;
+  const int np = parts_of_row(row, a) * kWarps * a.maxsub;
+  if (md.mode == kModeGreedy) {
     float bv = -INFINITY;
     int bi = INT_MAX;
     for (int k = threadIdx.x; k < np; k += kThreads) {
@@ -427,148 +546,233 @@ __global__ void __launch_bounds__(kThreads, 4) sample_kernel(SampleArgs a) {
     for (int o = 16; o > 0; o >>= 1)
       merge_max(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
     if (lane == 0) {
-      red_f[warp] = bv;
-      red_i[warp] = bi;
+      sm.red_f[warp] = bv;
+      sm.red_i[warp] = bi;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      for (int w = 1; w < kWarps; ++w) merge_max(bv, bi, red_f[w], red_i[w]);
+      for (int w = 1; w < kWarps; ++w) merge_max(bv, bi, sm.red_f[w], sm.red_i[w]);
       a.out[row] = bi == INT_MAX ? 0 : bi;
     }
   } else {
-    // Global max of the partials.
+    // Each thread a contiguous run of partials (held in registers when short).
+    constexpr int kRun = 4;
+    const int pp = (np + kThreads - 1) / kThreads;
+    const int k0 = min(int(threadIdx.x) * pp, np), k1 = min(k0 + pp, np);
+    float2 run[kRun];
     float gm = -INFINITY;
-    for (int k = threadIdx.x; k < np; k += kThreads) gm = fmaxf(gm, __ldcg(rp + k).x);
+#pragma unroll
+    for (int j = 0; j < kRun; ++j) {
+      run[j] = k0 + j < k1 ? __ldcg(rp + k0 + j) : make_float2(-INFINITY, 0.f);
+      gm = fmaxf(gm, run[j].x);
+    }
+    for (int k = k0 + kRun; k < k1; ++k) gm = fmaxf(gm, __ldcg(rp + k).x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
-    if (lane == 0) red_f[warp] = gm;
+    if (lane == 0) sm.red_f[warp] = gm;
     __syncthreads();
-    gm = red_f[0];
+    gm = sm.red_f[0];
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) gm = fmaxf(gm, red_f[w]);
-    // Each thread owns a contiguous run of partials; their weights s * 2^(m - gm) in fp64.
-    const int pp = (np + kThreads - 1) / kThreads;
-    const int k0 = threadIdx.x * pp, k1 = min(k0 + pp, np);
+    for (int w = 1; w < kWarps; ++w) gm = fmaxf(gm, sm.red_f[w]);
+    auto pweight = [&](float2 p) {
+      return p.x == -INFINITY || p.y <= 0.f ? 0.0 : double(p.y) * double(ex2(p.x - gm));
+    };
     double wsum = 0.0;
-    for (int k = k0; k < k1; ++k) {
-      const float2 p = __ldcg(rp + k);
-      if (p.x != -INFINITY) wsum += double(p.y) * double(fast_exp2(p.x - gm));
-    }
+#pragma unroll
+    for (int j = 0; j < kRun; ++j) wsum += pweight(run[j]);
+    for (int k = k0 + kRun; k < k1; ++k) wsum += pweight(__ldcg(rp + k));
     double total;
-    const double before = block_exclusive_scan(wsum, warp_sums, &total);
-    const uint4 r = philox4x32_10(make_uint4(unsigned(row), 0u, unsigned(s_rng[1]), unsigned(s_rng[1] >> 32)),
-                                  unsigned(s_rng[0]), unsigned(s_rng[0] >> 32));
+    const double before = block_exclusive_scan(wsum, sm.warp_sums, &total);
+    const uint4 r = philox4x32_10(make_uint4(unsigned(row), 0u, unsigned(sm.rng[1]), unsigned(sm.rng[1] >> 32)),
+                                  unsigned(sm.rng[0]), unsigned(sm.rng[0] >> 32));
     const double u = double((uint64_t(r.x) << 21) | (r.y >> 11)) * 0x1p-53;  // [0, 1)
     const double target = u * total;
     // The partial whose interval [before_k, before_k + w_k) holds the target.
-    const int owner = block_claimer(gm != -INFINITY && wsum > 0.0, before, target, red_i);
+    const int owner = block_claimer(gm != -INFINITY && wsum > 0.0, before, target, sm.red_i);
     if (threadIdx.x == owner) {
       double acc = before;
       int kk = -1;
       double rest = INFINITY;  // past the run's last weight (rounding): its last token
-      for (int k = k0; k < k1; ++k) {
-        const float2 p = __ldcg(rp + k);
-        if (p.x == -INFINITY || p.y <= 0.f) continue;
-        const double w = double(p.y) * double(fast_exp2(p.x - gm));
-        if (w <= 0.0) continue;
+      bool done = false;
+      auto step = [&](int k, float2 pk) {
+        const double w = pweight(pk);
+        if (done || w <= 0.0) return;
         kk = k;
         if (target < acc + w) {
           rest = target - acc;
-          break;
+          done = true;
+        } else {
+          acc += w;
         }
-        acc += w;
-      }
-      s_flag = kk;
-      s_target = rest;
+      };
+#pragma unroll
+      for (int j = 0; j < kRun; ++j)
+        if (k0 + j < k1) step(k0 + j, run[j]);
+      for (int k = k0 + kRun; k < k1 && !done; ++k) step(k, __ldcg(rp + k));
+      sm.flag = kk;
+      sm.target = rest;
     }
     __syncthreads();
-    const int ks = owner < 0 ? -1 : s_flag;
+    const int ks = owner < 0 ? -1 : sm.flag;
     if (ks < 0) {  // every logit is -inf: nothing to draw from
       if (threadIdx.x == 0) a.out[row] = 0;
     } else {
-      // Rescan sub-chunk ks in vocabulary order: each thread a contiguous run of groups.
-      const int64_t rlo = int64_t(ks / kWarps) * a.chunk + int64_t(ks % kWarps) * sub;
-      const int64_t rhi = min(rlo + sub, min(int64_t(ks / kWarps) * a.chunk + a.chunk, a.vocab));
-      if (md.pen_on) build_bitmap(a, row, rlo, rhi - rlo, bitmap);
+      // Rescan run ks in vocabulary order: each thread a contiguous stretch of groups.
+      int64_t plo, phi, wlo, whi;
+      part_cols(a, row, ks / (kWarps * a.maxsub), plo, phi);
+      warp_cols(plo, phi, (ks / a.maxsub) % kWarps, wlo, whi);
+      const int64_t rlo = min(wlo + int64_t(ks % a.maxsub) * kSubCols, whi), rhi = min(rlo + kSubCols, whi);
+      if (md.pen_on) {  // the run's presence bits, as the partials kernel stored them
+        for (int64_t w = rlo / 32 + threadIdx.x; w < (rhi + 31) / 32; w += kThreads)
+          bitmap[w - rlo / 32] = __ldcg(a.presence + int64_t(row) * a.pwords + w);
+        __syncthreads();
+      }
       const int64_t len = rhi - rlo;
       const int64_t per = ((len + int64_t(kThreads) * VE - 1) / (int64_t(kThreads) * VE)) * VE;
-      const int64_t t0 = rlo + threadIdx.x * per, t1 = min(t0 + per, rhi);
+      const int64_t t0 = min(rlo + threadIdx.x * per, rhi), t1 = min(t0 + per, rhi);
       double local = 0.0;
-      for (int64_t i = t0; i < t1; i += VE) {
-        float v[VE];
-        const int n = load_group<T>(lrow, i, t1, a.vec_ok, v);
-        const uint32_t bits = md.pen_on ? presence_bits(bitmap, i - rlo, VE) : 0u;
+      constexpr int kG = 8;  // groups of a stretch loaded at once (a stretch is at most 8 groups)
+      for (int64_t ib = t0; ib < t1; ib += kG * VE) {
+        uint4 raw[kG];
 #pragma unroll
-        for (int e = 0; e < VE; ++e)
-          if (e < n) local += double(weight<T>(md.pen_on ? penalize<true>(v[e], bits, e, md.pen) : v[e], md, gm));
-      }
-      double rtotal;
-      const double rbefore = block_exclusive_scan(local, warp_sums, &rtotal);
-      const double tt = s_target;
-      const int rowner = block_claimer(local > 0.0, rbefore, tt, red_i);
-      if (threadIdx.x == rowner) {
-        double acc = rbefore;
-        int pick = -1;
-        for (int64_t i = t0; i < t1 && !(pick >= 0 && tt < acc); i += VE) {
+        for (int g = 0; g < kG; ++g) {
+          const int64_t i = ib + g * VE;
+          raw[g] = a.vec_ok && i + VE <= t1 ? ldg_nc_v4(lrow + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+          const int64_t i = ib + g * VE;
+          if (i >= t1) continue;
           float v[VE];
-          const int n = load_group<T>(lrow, i, t1, a.vec_ok, v);
+          int n = VE;
+          if (a.vec_ok && i + VE <= t1) unpack16<T>(raw[g], v);
+          else n = load_group<T>(lrow, i, t1, a.vec_ok, v);
           const uint32_t bits = md.pen_on ? presence_bits(bitmap, i - rlo, VE) : 0u;
 #pragma unroll
-          for (int e = 0; e < VE; ++e) {
-            if (e >= n || (pick >= 0 && tt < acc)) continue;
-            const float ev = weight<T>(md.pen_on ? penalize<true>(v[e], bits, e, md.pen) : v[e], md, gm);
-            if (ev > 0.f) {
-              acc += double(ev);
-              pick = int(i + e);  // the first token whose cumulative weight passes tt, else the last
-            }
-          }
+          for (int e = 0; e < VE; ++e)
+            if (e < n) local += double(weight<T>(md.pen_on ? penalize<true>(v[e], bits, e, md.pen) : v[e], md, gm));
         }
-        a.out[row] = pick;
-      } else if (rowner < 0 && threadIdx.x == 0) {
-        a.out[row] = rlo;  // unreachable while the partial had weight; keeps the output defined
+      }
+      double rtotal;
+      const double rbefore = block_exclusive_scan(local, sm.warp_sums, &rtotal);
+      const double tt = sm.target;
+      const int rowner = block_claimer(local > 0.0, rbefore, tt, sm.red_i);
+      if (threadIdx.x == rowner) sm.obefore = rbefore;
+      __syncthreads();
+      if (rowner < 0) {
+        if (threadIdx.x == 0) a.out[row] = rlo;  // unreachable while the partial had weight
+      } else if (warp == 0) {
+        // The owner's stretch walked by warp 0, two elements a lane.
+        const int64_t o0 = min(rlo + int64_t(rowner) * per, rhi), o1 = min(o0 + per, rhi);
+        int pick = -1;
+        double acc = sm.obefore;
+        auto elem_weight = [&](int64_t i) {
+          const int64_t g = (i - rlo) & ~int64_t(VE - 1);
+          const uint32_t bits = md.pen_on ? presence_bits(bitmap, g, VE) : 0u;
+          const float l = Elem<T>::to_f(lrow[i]);
+          return weight<T>(md.pen_on ? penalize<true>(l, bits, int((i - rlo) - g), md.pen) : l, md, gm);
+        };
+        for (int64_t base = o0; base < o1 && pick < 0; base += 64) {
+          float w2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int64_t i = base + 2 * lane + e;
+            w2[e] = i < o1 ? elem_weight(i) : 0.f;
+          }
+          const double mine = double(w2[0]) + double(w2[1]);
+          double incl = mine;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const double y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          const double excl = acc + incl - mine;
+          // the first element whose cumulative weight passes tt
+          int cand = INT_MAX;
+          if (w2[0] > 0.f && tt < excl + double(w2[0])) cand = 2 * lane;
+          else if (w2[1] > 0.f && tt < excl + mine) cand = 2 * lane + 1;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
+          if (cand != INT_MAX) pick = int(base + cand);
+          acc += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (pick < 0) {  // rounding past the stretch's own total: its last token with weight
+          int last = -1;
+          for (int64_t i = o0 + lane; i < o1; i += 32)
+            if (elem_weight(i) > 0.f) last = int(i);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+          pick = last >= 0 ? last : int(o0);
+        }
+        if (lane == 0) a.out[row] = pick;
       }
     }
   }
   if (threadIdx.x == 0) {
-    a.tickets[row] = 0u;
     __threadfence();
-    if (atomicAdd(a.tickets + a.num_rows, 1u) == unsigned(a.num_rows - 1)) {
-      a.rng[1] = s_rng[1] + 1ull;
-      a.tickets[a.num_rows] = 0u;
+    if (atomicAdd(a.ctl, 1u) == unsigned(a.num_rows - 1)) {  // every CTA has read the offset
+      a.rng[1] = sm.rng[1] + 1ull;
+      a.ctl[0] = 0u;
     }
   }
 }
 
+// One wave of resident CTAs (4 per SM) over the whole batch, each span at least 2048 columns and
+// twice the token-table length (every part re-reads its row's table), at most kMaxPart columns.
 struct SamplePlan {
-  int chunk, nsplit;
+  int64_t vp, per;
+  unsigned grid;
 };
 
-// Vocabulary chunks per row: about four CTAs per SM over the batch, at most 24 per row (each
-// chunk re-reads the row's token table), at least what the shared-memory bitmap allows.
-// Measured on B200 (151,936-token rows): 256 rows best at 5 chunks, 64 at 9-10, 8 at 20-40.
-SamplePlan plan_sample(int num_rows, int64_t vocab, int num_sms) {
-  const int64_t nmin = (vocab + kMaxChunk - 1) / kMaxChunk, nmax = (vocab + kMinChunk - 1) / kMinChunk;
-  int64_t n = (int64_t(num_sms) * 4 + num_rows - 1) / num_rows;
-  n = std::min<int64_t>(std::min<int64_t>(n, 24), nmax);
-  n = std::max(n, nmin);
-  const int64_t chunk = std::max<int64_t>(((vocab + n - 1) / n + 255) / 256 * 256, kMinChunk);
-  return SamplePlan{int(chunk), int((vocab + chunk - 1) / chunk)};
+SamplePlan plan_sample(int num_rows, int64_t vocab, int64_t table_len, int num_sms) {
+  const int64_t vp = (vocab + 255) / 256 * 256, total = int64_t(num_rows) * vp;
+  int64_t per = (total + int64_t(num_sms) * 4 - 1) / (int64_t(num_sms) * 4);
+  per = std::max<int64_t>(per, std::max<int64_t>(kMinPart, 2 * table_len));
+  per = std::min<int64_t>((per + 255) / 256 * 256, kMaxPart);
+  return SamplePlan{vp, per, unsigned((total + per - 1) / per)};
 }
 
-size_t tickets_bytes(int num_rows) { return (size_t(num_rows + 1) * sizeof(unsigned) + 255) / 256 * 256; }
+int max_parts(int64_t vocab) { return int(((vocab + 255) / 256 * 256 + kMinPart - 1) / kMinPart + 2); }
+// Sub-run partials per warp run: runs are at most ceil(per / 256) * 32 columns.
+int max_sub(int64_t per) { return int(((per + 255) / 256 * 32 + kSubCols - 1) / kSubCols); }
+constexpr int kMaxSub = (kMaxPart / 256 * 32 + kSubCols - 1) / kSubCols;  // for per = kMaxPart
+
+constexpr size_t kCtlBytes = 256;  // {grid ticket, penalty flag}, padded
+size_t partials_bytes(int num_rows, int64_t vocab) {
+  return (size_t(num_rows) * size_t(max_parts(vocab)) * kWarps * kMaxSub * sizeof(float2) + 255) / 256 * 256;
+}
+
+// The partials kernel, then the finish kernel as its programmatic dependent (its launch and row
+// parameters overlap the partials kernel's tail; griddepcontrol.wait orders the rest).
+template <typename T>
+cudaError_t launch_pair(const SampleArgs& a, unsigned grid, int num_rows, cudaStream_t stream) {
+  sample_partials_kernel<T><<<grid, kThreads, 0, stream>>>(a);
+  cudaError_t ce = cudaGetLastError();
+  if (ce != cudaSuccess) return ce;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(num_rows));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, sample_finish_kernel<T>, a);
+}
 
 }  // namespace
 
 size_t sample_workspace_size(int num_rows, int64_t vocab) {
-  const int64_t max_splits = (vocab + kMinChunk - 1) / kMinChunk;
-  return tickets_bytes(num_rows) + size_t(num_rows) * size_t(max_splits) * kWarps * sizeof(float2);
+  return kCtlBytes + partials_bytes(num_rows, vocab) + size_t(num_rows) * size_t((vocab + 31) / 32) * 4;
 }
 
 cudaError_t launch_sample(const void* logits, int64_t row_stride, int num_rows, int64_t vocab, int dtype,
                           const float* temps, const float* pens, const int64_t* table, int64_t table_stride,
                           int64_t table_len, unsigned long long* rng, int64_t* out, void* workspace,
                           cudaStream_t stream) {
-  const SamplePlan plan = plan_sample(num_rows, vocab, device_sm_count());
+  const SamplePlan plan = plan_sample(num_rows, vocab, table_len, device_sm_count());
   SampleArgs a;
   a.logits = logits;
   a.row_stride = row_stride;
@@ -581,19 +785,21 @@ cudaError_t launch_sample(const void* logits, int64_t row_stride, int num_rows, 
   a.table_len = table_len;
   a.rng = rng;
   a.out = out;
-  a.tickets = static_cast<unsigned*>(workspace);
-  a.partials = reinterpret_cast<float2*>(static_cast<char*>(workspace) + tickets_bytes(num_rows));
-  a.chunk = plan.chunk;
-  a.nsplit = plan.nsplit;
+  a.ctl = static_cast<unsigned*>(workspace);
+  a.partials = reinterpret_cast<float2*>(static_cast<char*>(workspace) + kCtlBytes);
+  a.presence = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + kCtlBytes + partials_bytes(num_rows, vocab));
+  a.pwords = (vocab + 31) / 32;
+  a.vp = plan.vp;
+  a.per = plan.per;
+  a.maxparts = max_parts(vocab);
+  a.maxsub = max_sub(plan.per);
   const int es = dtype == FVB_DTYPE_F32 ? 4 : 2;
   a.vec_ok = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && (row_stride * es) % 16 == 0;
-  const unsigned grid = unsigned(int64_t(num_rows) * plan.nsplit);
   switch (dtype) {
-    case FVB_DTYPE_F32: sample_kernel<float><<<grid, kThreads, 0, stream>>>(a); break;
-    case FVB_DTYPE_BF16: sample_kernel<__nv_bfloat16><<<grid, kThreads, 0, stream>>>(a); break;
-    default: sample_kernel<__half><<<grid, kThreads, 0, stream>>>(a); break;
+    case FVB_DTYPE_F32: return launch_pair<float>(a, plan.grid, num_rows, stream);
+    case FVB_DTYPE_BF16: return launch_pair<__nv_bfloat16>(a, plan.grid, num_rows, stream);
+    default: return launch_pair<__half>(a, plan.grid, num_rows, stream);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace fvb

@@ -340,7 +340,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("QKNormRopeStoreCuda", &QKNormRopeStoreCuda,
         "fused q/k RMSNorm + rotary embedding + KV-cache write; returns q as (n_heads, num_tokens, d_head)");
   m.def("SampleTokensCuda", &SampleTokensCuda,
-        "next-token ids: presence penalty, greedy argmax / temperature sampling (one launch)", py::arg("logits"),
+        "next-token ids: presence penalty, greedy argmax / temperature sampling (one pass over the logits)", py::arg("logits"),
         py::arg("temperatures"), py::arg("presence_penalties") = py::none(), py::arg("token_table") = py::none(),
         py::arg("rng_state"), py::arg("workspace") = py::none());
   m.def("SampleWorkspaceSize", &SampleWorkspaceSize, "workspace bytes of SampleTokensCuda");

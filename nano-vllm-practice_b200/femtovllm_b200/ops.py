@@ -258,7 +258,7 @@ def sample_tokens(
     rng_state: torch.Tensor | None = None,
     workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Next-token ids ``(B,)`` int64 from ``logits`` ``(B, vocab)``, on the device, in one launch.
+    """Next-token ids ``(B,)`` int64 from ``logits`` ``(B, vocab)``, on the device (one pass over the logits).
 
     The arithmetic of the reference's ``Sampler.forward`` (``femtovllm/engine/sampler.py:15-114``):
     when any ``|presence_penalties| > 1e-5``, every token that occurs in a row of ``token_table``
