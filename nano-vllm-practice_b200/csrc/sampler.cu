@@ -1,5 +1,5 @@
-// Next-token sampling over a batch of logit rows in one launch: presence
-// penalty, greedy argmax and temperature sampling.
+// Next-token sampling over a batch of logit rows in one pass over the logits:
+// presence penalty, greedy argmax and temperature sampling.
 //
 // The reference's Sampler.forward (femtovllm/engine/sampler.py:15-114) builds
 // Python lists of the sampling parameters, a padded token table and a
@@ -18,12 +18,13 @@
 //
 // Two launches.  sample_partials_kernel streams the logits once: one wave of CTAs, each owning
 // an equal span of the batch (one or more row parts); each of a CTA's 8 warps folds a
-// contiguous run of a part into a partial, (max, first index) for greedy rows or (m, s) with
-// s = sum 2^(x2 - m) in the log2 domain for sampled rows.  No CTA-wide barrier on that path
-// (only around the presence bitmap of penalised rows).  sample_finish_kernel, one CTA per
-// row, merges the row's partials, draws the Philox uniform, finds the run holding it and
-// rescans only that run (from L2) for the exact token; the last CTA to finish advances the
-// RNG offset, so a CUDA-graph replay draws fresh numbers.
+// contiguous run of a part into one partial per 2048 columns, (max, first index) for greedy
+// rows or (m, s) with s = sum 2^(x2 - m) in the log2 domain for sampled rows.  No CTA-wide
+// barrier on that path (only around the presence bitmap of penalised rows, whose words the
+// warps also store for the finish kernel).  sample_finish_kernel, one CTA per row and launched
+// as a programmatic dependent of the first, merges the row's partials, draws the Philox uniform,
+// finds the 2048-column run holding it and rescans only that run for the exact token; the last
+// CTA to finish advances the RNG offset, so a CUDA-graph replay draws fresh numbers.
 #include <algorithm>
 
 #include "common.cuh"
