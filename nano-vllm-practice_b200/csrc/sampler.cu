@@ -202,18 +202,18 @@ __device__ __forceinline__ void lane_reset(Lane& st) {
   st.pbase = -1;
 }
 
-// Folds one 16-byte vector (columns i..i+VE-1; entries past the range are -inf) into a lane.
-// Greedy rows penalise every element.  Sampled rows on the fp32 path weigh the raw logits and
-// sum the weights of penalised tokens apart: 2^((l - p) c - m) = 2^(l c - m) * 2^(-p c), so the
-// penalty becomes one factor at the end instead of work on every element.  Sampled rows rescale
-// lazily: m moves only when a vector's maximum passes it by more than 8 (weights stay below 2^8;
-// a negative penalty lifts penalised weights by 2^(|p| c) on top).  The row's treatment is a
-// warp-uniform branch.
-template <typename T>
+// Folds one 16-byte vector (columns i..i+VE-1; entries past the range are -inf) into a lane.  The
+// row's treatment (MODE, PEN) is a template parameter: each warp run calls the loop built for its
+// row, so the per-vector code carries no mode tests.  Greedy rows penalise every element.  Sampled
+// rows on the fp32 path weigh the raw logits and sum the weights of penalised tokens apart:
+// 2^((l - p) c - m) = 2^(l c - m) * 2^(-p c), so the penalty becomes one factor per partial.
+// Sampled rows rescale lazily: m moves only when a vector's maximum passes it by more than 8
+// (weights stay below 2^8; a negative penalty lifts penalised weights by 2^(|p| c) on top).
+template <typename T, int MODE, bool PEN>
 __device__ __forceinline__ void consume(float* x, uint32_t bits, int i, const RowMode& md, Lane& st) {
   constexpr int VE = 16 / sizeof(T);
-  if (md.mode == kModeGreedy) {
-    if (md.pen_on) {
+  if constexpr (MODE == kModeGreedy) {
+    if constexpr (PEN) {
 #pragma unroll
       for (int e = 0; e < VE; ++e) x[e] = penalize<true>(x[e], bits, e, md.pen);
     }
@@ -226,105 +226,100 @@ __device__ __forceinline__ void consume(float* x, uint32_t bits, int i, const Ro
       st.pa = g;
       st.pbase = k;  // the first column holding the new maximum
     }
-    return;
-  }
-  float scale = md.c;
-  if (md.mode == kModeSampleRounded) {
+  } else {
+    float scale = md.c;
+    if constexpr (MODE == kModeSampleRounded) {
 #pragma unroll
-    for (int e = 0; e < VE; ++e) x[e] = rounded_quotient<T>(x[e], md);
-    scale = kLog2e;
-  }
-  const float gy = tree_max<VE>(x) * scale;  // scale > 0: the max commutes with it
-  if (gy > st.pa + 8.f) {
-    const float f = ex2(st.pa - gy);  // 0 while pa is -inf
+      for (int e = 0; e < VE; ++e) x[e] = rounded_quotient<T>(x[e], md);
+      scale = kLog2e;
+    }
+    const float gy = tree_max<VE>(x) * scale;  // scale > 0: the max commutes with it
+    if (gy > st.pa + 8.f) {
+      const float f = ex2(st.pa - gy);  // 0 while pa is -inf
 #pragma unroll
-    for (int q = 0; q < 4; ++q) st.acc[q] *= f;
-    st.accp *= f;
-    st.pa = gy;
-  }
-  if (st.pa == -INFINITY) return;
+      for (int q = 0; q < 4; ++q) st.acc[q] *= f;
+      st.accp *= f;
+      st.pa = gy;
+    }
+    if (st.pa == -INFINITY) return;
 #pragma unroll
-  for (int e = 0; e < VE; ++e) {
-    const float w = ex2(fmaf(x[e], scale, -st.pa));
-    st.acc[e & 3] += w;
-    if (bits & (1u << e)) st.accp += w;
+    for (int e = 0; e < VE; ++e) {
+      const float w = ex2(fmaf(x[e], scale, -st.pa));
+      st.acc[e & 3] += w;
+      if constexpr (PEN) {
+        if (bits & (1u << e)) st.accp += w;
+      }
+    }
   }
 }
 
 // Reduces the warp's lanes to one partial and writes it (lane 0): greedy (value, first index);
 // sampled (m, s) with the penalty factor applied.
+template <int MODE, bool PEN>
 __device__ __forceinline__ void emit(const Lane& st, const RowMode& md, float2* dst) {
-  const bool greedy = md.mode == kModeGreedy;
+  constexpr bool greedy = MODE == kModeGreedy;
   float pa = st.pa, pb = 0.f;
   int pi = INT_MAX;
-  if (greedy) {
+  if constexpr (greedy) {
     pi = st.pbase >= 0 ? st.pbase : INT_MAX;
   } else {
     pb = (st.acc[0] + st.acc[1]) + (st.acc[2] + st.acc[3]);
-    if (md.pen_on) pb = fmaxf(0.f, fmaf(md.kpen, st.accp, pb));
+    if constexpr (PEN) pb = fmaxf(0.f, fmaf(md.kpen, st.accp, pb));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float a2 = __shfl_xor_sync(0xffffffffu, pa, o);
-    const float b2 = __shfl_xor_sync(0xffffffffu, pb, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, pi, o);
-    if (greedy) merge_max(pa, pi, a2, i2);
-    else merge_lse(pa, pb, a2, b2);
+    if constexpr (greedy) {
+      merge_max(pa, pi, a2, __shfl_xor_sync(0xffffffffu, pi, o));
+    } else {
+      merge_lse(pa, pb, a2, __shfl_xor_sync(0xffffffffu, pb, o));
+    }
   }
   if ((threadIdx.x & 31) == 0) *dst = make_float2(pa, greedy ? __int_as_float(pi) : pb);
 }
 
 // One warp's run [lo, hi) of a row, one partial per kSubCols columns (maxsub partials written,
-// empty ones neutral).  Warp-uniform loop, software-pipelined: while a lane folds its U current
-// 16-byte vectors the next U are in flight.  Column indices are 32-bit (vocab < 2^31).  Not with
-// 16-byte vectors when the row is not 16-byte aligned (vec_ok false): every load goes through the
-// bounded scalar path.
-template <typename T>
+// empty ones neutral).  Warp-uniform loop with U 16-byte loads in flight per lane; a countdown
+// marks the partial boundaries.  Column indices are 32-bit (vocab < 2^31).  When the row is not
+// 16-byte aligned (vec_ok false) every load goes through the bounded scalar path.
+template <typename T, int MODE, bool PEN>
 __device__ __forceinline__ void pass1(const T* lrow, int lo, int hi, int c0, bool vec_ok, const uint32_t* bitmap,
                                       const RowMode& md, float2* dst, int maxsub) {
-  constexpr int VE = 16 / sizeof(T), U = 2, STEP = 32 * VE, IT = U * STEP;
+  constexpr int VE = 16 / sizeof(T), U = 4, STEP = 32 * VE, IT = U * STEP;
   static_assert(kSubCols % IT == 0, "sub-runs are whole iterations");
   const int lane = threadIdx.x & 31;
   Lane st;
   lane_reset(st);
   int sub = 0, emitted = lo;  // partials written; columns covered by them end at `emitted`
-  int ib = lo;  // warp-uniform column of the current iteration
-  if (vec_ok && ib + IT <= hi) {
-    uint4 cur[U];
+  int ib = lo;                // warp-uniform column of the current iteration
+  if (vec_ok) {
+    int left = kSubCols;
+    for (; ib + IT <= hi; ib += IT) {
+      uint4 raw[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) cur[u] = ldg_nc_v4(lrow + ib + u * STEP + lane * VE);
-    while (true) {
-      const int nb = ib + IT;
-      const bool more = nb + IT <= hi;
-      uint4 nxt[U];
-      if (more) {
-#pragma unroll
-        for (int u = 0; u < U; ++u) nxt[u] = ldg_nc_v4(lrow + nb + u * STEP + lane * VE);
-      }
+      for (int u = 0; u < U; ++u) raw[u] = ldg_nc_v4(lrow + ib + u * STEP + lane * VE);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int i = ib + u * STEP + lane * VE;
         float x[VE];
-        unpack16<T>(cur[u], x);
-        const uint32_t bits = md.pen_on ? presence_bits(bitmap, i - c0, VE) : 0u;
-        consume<T>(x, bits, i, md, st);
+        unpack16<T>(raw[u], x);
+        const uint32_t bits = PEN ? presence_bits(bitmap, i - c0, VE) : 0u;
+        consume<T, MODE, PEN>(x, bits, i, md, st);
       }
-      ib = nb;
-      if ((ib - lo) % kSubCols == 0) {
-        emit(st, md, dst + sub);
+      left -= IT;
+      if (left == 0) {
+        emit<MODE, PEN>(st, md, dst + sub);
         ++sub;
-        emitted = ib;
+        emitted = ib + IT;
+        left = kSubCols;
         lane_reset(st);
       }
-      if (!more) break;
-#pragma unroll
-      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
     }
   }
   // The rest, one vector per lane at a time with bounds.
   for (; ib < hi; ib += STEP) {
     if (ib > emitted && (ib - lo) % kSubCols == 0 && sub < maxsub) {
-      emit(st, md, dst + sub);
+      emit<MODE, PEN>(st, md, dst + sub);
       ++sub;
       emitted = ib;
       lane_reset(st);
@@ -337,16 +332,16 @@ __device__ __forceinline__ void pass1(const T* lrow, int lo, int hi, int c0, boo
 #pragma unroll
       for (int e = 0; e < VE; ++e) x[e] = -INFINITY;
     }
-    const uint32_t bits = md.pen_on && i < hi ? presence_bits(bitmap, i - c0, VE) : 0u;
-    consume<T>(x, bits, i, md, st);
+    const uint32_t bits = PEN && i < hi ? presence_bits(bitmap, i - c0, VE) : 0u;
+    consume<T, MODE, PEN>(x, bits, i, md, st);
   }
   if (hi > emitted && sub < maxsub) {  // the last, partial sub-run
-    emit(st, md, dst + sub);
+    emit<MODE, PEN>(st, md, dst + sub);
     ++sub;
   }
   if (lane == 0)
-    for (; sub < maxsub; ++sub) dst[sub] = md.mode == kModeGreedy ? make_float2(-INFINITY, __int_as_float(INT_MAX))
-                                                                  : make_float2(-INFINITY, 0.f);
+    for (; sub < maxsub; ++sub)
+      dst[sub] = MODE == kModeGreedy ? make_float2(-INFINITY, __int_as_float(INT_MAX)) : make_float2(-INFINITY, 0.f);
 }
 
 // Marks in `bitmap` the tokens of row `row`'s table that fall in [lo, lo + len): the table
@@ -496,8 +491,15 @@ __global__ void __launch_bounds__(kThreads, 4) sample_partials_kernel(SampleArgs
     const T* lrow = static_cast<const T*>(a.logits) + row * a.row_stride;
     int64_t wlo, whi;
     warp_cols(lo, hi, warp, wlo, whi);
-    pass1<T>(lrow, int(wlo), int(whi), int(lo), a.vec_ok, bitmap, md,
-             a.partials + ((row * a.maxparts + slot) * kWarps + warp) * a.maxsub, a.maxsub);
+    float2* dst = a.partials + ((row * a.maxparts + slot) * kWarps + warp) * a.maxsub;
+    const int wl = int(wlo), wh = int(whi), c0 = int(lo);
+    switch (md.mode * 2 + int(md.pen_on)) {  // pen_on implies the fp32 path for sampled rows
+      case 0: pass1<T, kModeGreedy, false>(lrow, wl, wh, c0, a.vec_ok, bitmap, md, dst, a.maxsub); break;
+      case 1: pass1<T, kModeGreedy, true>(lrow, wl, wh, c0, a.vec_ok, bitmap, md, dst, a.maxsub); break;
+      case 2: pass1<T, kModeSampleF32, false>(lrow, wl, wh, c0, a.vec_ok, bitmap, md, dst, a.maxsub); break;
+      case 3: pass1<T, kModeSampleF32, true>(lrow, wl, wh, c0, a.vec_ok, bitmap, md, dst, a.maxsub); break;
+      default: pass1<T, kModeSampleRounded, false>(lrow, wl, wh, c0, a.vec_ok, bitmap, md, dst, a.maxsub); break;
+    }
     if (md.pen_on) {  // this warp's run of the bitmap, for the finish kernel's rescan
       uint32_t* dst = a.presence + row * a.pwords;
       for (int64_t w = wlo / 32 + lane; w < (whi + 31) / 32; w += 32) dst[w] = bitmap[w - lo / 32];
