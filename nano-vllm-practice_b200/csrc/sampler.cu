@@ -513,7 +513,7 @@ struct Shared {
   float red_f[kWarps];
   int red_i[kWarps];
   int flag;
-  double target, obefore;
+  double target;
   unsigned long long rng[2];
 };
 
@@ -620,94 +620,51 @@ __global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
     if (ks < 0) {  // every logit is -inf: nothing to draw from
       if (threadIdx.x == 0) a.out[row] = 0;
     } else {
-      // Rescan run ks in vocabulary order: each thread a contiguous stretch of groups.
+      // Rescan run ks in vocabulary order: each thread a contiguous stretch of kPer columns whose
+      // weights stay in registers; the logits and the presence words are fetched in one round trip.
+      constexpr int kPer = kSubCols / kThreads;
+      static_assert(kPer == 8 && kPer % VE == 0, "a stretch is whole 16-byte groups within one word");
       int64_t plo, phi, wlo, whi;
       part_cols(a, row, ks / (kWarps * a.maxsub), plo, phi);
       warp_cols(plo, phi, (ks / a.maxsub) % kWarps, wlo, whi);
       const int64_t rlo = min(wlo + int64_t(ks % a.maxsub) * kSubCols, whi), rhi = min(rlo + kSubCols, whi);
+      const int64_t t0 = min(rlo + int64_t(threadIdx.x) * kPer, rhi), t1 = min(t0 + kPer, rhi);
+      float v[kPer];
+#pragma unroll
+      for (int g = 0; g < kPer / VE; ++g) load_group<T>(lrow, t0 + g * VE, t1, a.vec_ok, v + g * VE);
       if (md.pen_on) {  // the run's presence bits, as the partials kernel stored them
         for (int64_t w = rlo / 32 + threadIdx.x; w < (rhi + 31) / 32; w += kThreads)
           bitmap[w - rlo / 32] = __ldcg(a.presence + int64_t(row) * a.pwords + w);
         __syncthreads();
       }
-      const int64_t len = rhi - rlo;
-      const int64_t per = ((len + int64_t(kThreads) * VE - 1) / (int64_t(kThreads) * VE)) * VE;
-      const int64_t t0 = min(rlo + threadIdx.x * per, rhi), t1 = min(t0 + per, rhi);
+      const uint32_t bits = md.pen_on && t0 < t1 ? presence_bits(bitmap, t0 - rlo, kPer) : 0u;
+      float w[kPer];
       double local = 0.0;
-      constexpr int kG = 8;  // groups of a stretch loaded at once (a stretch is at most 8 groups)
-      for (int64_t ib = t0; ib < t1; ib += kG * VE) {
-        uint4 raw[kG];
 #pragma unroll
-        for (int g = 0; g < kG; ++g) {
-          const int64_t i = ib + g * VE;
-          raw[g] = a.vec_ok && i + VE <= t1 ? ldg_nc_v4(lrow + i) : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int g = 0; g < kG; ++g) {
-          const int64_t i = ib + g * VE;
-          if (i >= t1) continue;
-          float v[VE];
-          int n = VE;
-          if (a.vec_ok && i + VE <= t1) unpack16<T>(raw[g], v);
-          else n = load_group<T>(lrow, i, t1, a.vec_ok, v);
-          const uint32_t bits = md.pen_on ? presence_bits(bitmap, i - rlo, VE) : 0u;
-#pragma unroll
-          for (int e = 0; e < VE; ++e)
-            if (e < n) local += double(weight<T>(md.pen_on ? penalize<true>(v[e], bits, e, md.pen) : v[e], md, gm));
-        }
+      for (int e = 0; e < kPer; ++e) {
+        w[e] = t0 + e < t1 ? weight<T>(md.pen_on ? penalize<true>(v[e], bits, e, md.pen) : v[e], md, gm) : 0.f;
+        local += double(w[e]);
       }
       double rtotal;
       const double rbefore = block_exclusive_scan(local, sm.warp_sums, &rtotal);
       const double tt = sm.target;
       const int rowner = block_claimer(local > 0.0, rbefore, tt, sm.red_i);
-      if (threadIdx.x == rowner) sm.obefore = rbefore;
-      __syncthreads();
       if (rowner < 0) {
         if (threadIdx.x == 0) a.out[row] = rlo;  // unreachable while the partial had weight
-      } else if (warp == 0) {
-        // The owner's stretch walked by warp 0, two elements a lane.
-        const int64_t o0 = min(rlo + int64_t(rowner) * per, rhi), o1 = min(o0 + per, rhi);
-        int pick = -1;
-        double acc = sm.obefore;
-        auto elem_weight = [&](int64_t i) {
-          const int64_t g = (i - rlo) & ~int64_t(VE - 1);
-          const uint32_t bits = md.pen_on ? presence_bits(bitmap, g, VE) : 0u;
-          const float l = Elem<T>::to_f(lrow[i]);
-          return weight<T>(md.pen_on ? penalize<true>(l, bits, int((i - rlo) - g), md.pen) : l, md, gm);
-        };
-        for (int64_t base = o0; base < o1 && pick < 0; base += 64) {
-          float w2[2];
+      } else if (threadIdx.x == rowner) {
+        // The first column whose cumulative weight passes tt; rounding past the stretch's own
+        // total leaves the last column with weight.
+        double acc = rbefore;
+        int64_t pick = t0;
+        bool done = false;
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int64_t i = base + 2 * lane + e;
-            w2[e] = i < o1 ? elem_weight(i) : 0.f;
-          }
-          const double mine = double(w2[0]) + double(w2[1]);
-          double incl = mine;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const double y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-          }
-          const double excl = acc + incl - mine;
-          // the first element whose cumulative weight passes tt
-          int cand = INT_MAX;
-          if (w2[0] > 0.f && tt < excl + double(w2[0])) cand = 2 * lane;
-          else if (w2[1] > 0.f && tt < excl + mine) cand = 2 * lane + 1;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
-          if (cand != INT_MAX) pick = int(base + cand);
-          acc += __shfl_sync(0xffffffffu, incl, 31);
+        for (int e = 0; e < kPer; ++e) {
+          if (done || w[e] <= 0.f) continue;
+          acc += double(w[e]);
+          pick = t0 + e;
+          done = tt < acc;
         }
-        if (pick < 0) {  // rounding past the stretch's own total: its last token with weight
-          int last = -1;
-          for (int64_t i = o0 + lane; i < o1; i += 32)
-            if (elem_weight(i) > 0.f) last = int(i);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
-          pick = last >= 0 ? last : int(o0);
-        }
-        if (lane == 0) a.out[row] = pick;
+        a.out[row] = pick;
       }
     }
   }
