@@ -46,6 +46,16 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def _sustained_tflops():
+    """cuBLAS bf16 throughput held for seconds under the power cap (the denominator for a kernel
+    timed over a long back-to-back loop, as the prefill workloads are); None without the file."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        v = json.loads(p.read_text()).get("bf16_tflops_sustained")
+        return float(v) if v else None
+    return 1400.0
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle-reason sampling during the timed region."""
 
@@ -541,6 +551,9 @@ def run_other(args, rank, world, local_rank, hbm_peak, tflops_peak, peak_src):
             "pct_tensor_peak": round(100 * flops / (t * 1e-3) / 1e12 / (tflops_peak * world), 2),
             "pct_hbm_peak": round(100 * nbytes / (t * 1e-3) / 1e9 / (hbm_peak * world), 2),
             "peak_source": peak_src, "config": batch.name, "clocks": clk.summary()}
+    sus = _sustained_tflops()
+    if flops and sus:
+        line["pct_tensor_peak_sustained"] = round(100 * flops / (t * 1e-3) / 1e12 / (sus * world), 2)
     print(json.dumps(line), flush=True)
 
 
