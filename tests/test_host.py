@@ -75,6 +75,40 @@ def test_prefill_rejects_bad_arguments(lib):
     assert lib.fvb_paged_attention_prefill(*bad) == 1
 
 
+def _sample_args(**over):
+    """fvb_sample_tokens arguments with fake (never dereferenced) 256-byte aligned pointers."""
+    a = dict(logits=256, row_stride=1024, num_rows=4, vocab=1000, dtype=1, temps=256, pens=256, table=256,
+             table_stride=8, table_len=8, rng=256, out=256, ws=256, ws_bytes=1 << 20, stream=None)
+    a.update(over)
+    return [a[k] for k in ("logits", "row_stride", "num_rows", "vocab", "dtype", "temps", "pens", "table",
+                           "table_stride", "table_len", "rng", "out", "ws", "ws_bytes", "stream")]
+
+
+@pytest.mark.parametrize(
+    "over,status",
+    [
+        (dict(dtype=9), 2),                      # unsupported dtype
+        (dict(vocab=0), 1),                      # empty vocabulary
+        (dict(row_stride=999), 1),               # rows overlap
+        (dict(table=0), 1),                      # table_len > 0 without a table
+        (dict(table_stride=4), 1),               # table rows overlap
+        (dict(out=0), 1),                        # no output
+        (dict(ws_bytes=16), 4),                  # workspace too small
+        (dict(ws=264), 3),                       # workspace not 16-byte aligned
+        (dict(rng=260), 3),                      # rng state not 8-byte aligned
+        (dict(num_rows=0), 0),                   # empty batch: no-op
+    ],
+)
+def test_sample_rejects_bad_arguments_without_touching_the_device(lib, over, status):
+    assert lib.fvb_sample_tokens(*_sample_args(**over)) == status
+
+
+def test_sample_workspace_size(lib):
+    assert lib.fvb_sample_workspace_size(0, 1000) == 0
+    small = lib.fvb_sample_workspace_size(4, 1000)
+    assert small > 0 and lib.fvb_sample_workspace_size(256, 151936) > 64 * small
+
+
 def test_decode_workspace_plan(lib):
     # Plenty of (seq, kv head) units and short contexts: no split, no workspace.
     assert lib.fvb_paged_attention_decode_workspace_size(1024, 16, 8, 128, 512) == 0
