@@ -1,7 +1,11 @@
 // extern "C" entry points of libfemtovllm_b200.so (declared in
 // include/femtovllm_b200.h).  Host-side validation of every scalar argument,
 // the 16-byte alignment rules of the TMA / vector paths, workspace sizing,
-// and mapping of CUDA errors to fvb_status.  Nothing here allocates.
+// and mapping of CUDA errors to fvb_status.  Nothing here allocates.  Every compute entry point
+// opens an NVTX range named after itself, so Nsight Systems timelines and `ncu --nvtx` filters
+// see the library's calls (NVTX is a no-op unless a tool is attached).
+#include <nvtx3/nvToolsExt.h>
+
 #include <atomic>
 #include <cstdio>
 #include <cstring>
@@ -15,6 +19,14 @@ namespace fvb {
 __device__ int g_device_error[2] = {0, 0};
 
 namespace {
+
+// NVTX range for the lifetime of one entry-point call.
+struct TraceRange {
+  explicit TraceRange(const char* name) { nvtxRangePushA(name); }
+  ~TraceRange() { nvtxRangePop(); }
+  TraceRange(const TraceRange&) = delete;
+  TraceRange& operator=(const TraceRange&) = delete;
+};
 
 constexpr int kMaxDevices = 64;
 std::atomic<int*> g_err_ptr[kMaxDevices] = {};
@@ -242,6 +254,7 @@ int fvb_check_bounded_wait(int site, void* stream) {
 int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride, void* k_pool,
                       void* v_pool, int64_t num_blocks, const int64_t* slot_mapping, int64_t num_tokens,
                       int n_kv_heads, int head_dim, int block_size, int dtype, void* stream) {
+  TraceRange trace("fvb_store_kvcache");
   const int es = esize_of(dtype);
   if (es == 0) return FVB_ERR_UNSUPPORTED;
   if (num_tokens < 0 || n_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || num_blocks < 0 ||
@@ -262,6 +275,7 @@ int fvb_build_varlen_metadata(const int32_t* num_computed, const int32_t* num_ne
                               const int32_t* flat_blocks, int64_t num_flat_blocks, const int32_t* cu_blocks,
                               int max_blocks_per_seq, int64_t num_tokens, int32_t* positions, int32_t* cu_seqlens,
                               int32_t* kv_lens, int32_t* block_tables, int64_t* slot_mapping, void* stream) {
+  TraceRange trace("fvb_build_varlen_metadata");
   if (num_seqs <= 0 || num_tokens < 0 || max_blocks_per_seq < 0 || num_flat_blocks < 0 ||
       num_tokens >= (int64_t(1) << 31))
     return FVB_ERR_INVALID_ARGUMENT;
@@ -286,6 +300,7 @@ int fvb_qk_norm_rope_store(const void* q, int64_t q_token_stride, int64_t q_head
                            const int64_t* slot_mapping, int64_t num_tokens, int n_heads, int n_kv_heads,
                            int head_dim, void* q_out, void* k_pool, void* v_pool, int64_t num_blocks, int block_size,
                            int dtype, void* stream) {
+  TraceRange trace("fvb_qk_norm_rope_store");
   const int es = esize_of(dtype);
   if (es == 0) return FVB_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return FVB_ERR_UNSUPPORTED;
@@ -329,6 +344,7 @@ int fvb_sample_tokens(const void* logits, int64_t row_stride, int num_rows, int6
                       const float* temperatures, const float* presence_penalties, const int64_t* token_table,
                       int64_t table_stride, int64_t table_len, uint64_t* rng_state, int64_t* token_ids,
                       void* workspace, size_t workspace_bytes, void* stream) {
+  TraceRange trace("fvb_sample_tokens");
   const int es = esize_of(dtype);
   if (es == 0) return FVB_ERR_UNSUPPORTED;
   if (num_rows < 0 || vocab <= 0 || vocab >= (int64_t(1) << 31) || row_stride < vocab || table_len < 0 ||
@@ -353,6 +369,7 @@ int fvb_sample_tokens(const void* logits, int64_t row_stride, int num_rows, int6
 int fvb_build_slot_mapping(const int32_t* positions, int64_t num_tokens, const int32_t* cu_seqlens, int num_seqs,
                            const int32_t* block_tables, int max_blocks_per_seq, int block_size,
                            int64_t* slot_mapping, void* stream) {
+  TraceRange trace("fvb_build_slot_mapping");
   if (num_tokens < 0 || num_seqs < 0 || max_blocks_per_seq < 0 || block_size <= 0) return FVB_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return FVB_OK;
   if (!positions || !block_tables || !slot_mapping || num_seqs == 0) return FVB_ERR_INVALID_ARGUMENT;
@@ -393,6 +410,7 @@ int fvb_paged_attention_decode_strided(const void* q, int64_t q_token_stride, in
                                        int head_dim, int block_size, int num_seqs, const int32_t* block_tables,
                                        int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
                                        void* workspace, size_t workspace_bytes, void* stream) {
+  TraceRange trace("fvb_paged_attention_decode_strided");
   int st = check_attention(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
                            block_tables, max_blocks_per_seq, kv_lens, dtype);
   if (st) return st;
@@ -453,6 +471,7 @@ int fvb_paged_attention_prefill_strided(const void* q, int64_t q_token_stride, i
                                         const int32_t* cu_seqlens, int max_q_len, const int32_t* block_tables,
                                         int max_blocks_per_seq, const int32_t* kv_lens, const int32_t* positions,
                                         int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  TraceRange trace("fvb_paged_attention_prefill_strided");
   int st = check_attention(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, block_size, num_seqs,
                            block_tables, max_blocks_per_seq, kv_lens, dtype);
   if (st) return st;
