@@ -86,6 +86,31 @@ __device__ __forceinline__ void unpack16<__half>(const uint4& v, float* out) {
   }
 }
 
+// acc.x += lo(q) * lo(k) and acc.y += hi(q) * hi(k) for two packed 16-bit pairs, by
+// the mixed-precision FMA of sm_100 (fma.rn.f32.bf16 / .f16): the 16-bit operands are
+// taken as they are, the product is exact and rounded once, so the result equals an
+// fp32 FMA on the converted values without the conversion instructions.
+template <typename T>
+__device__ __forceinline__ void fma_pair16(uint32_t q, uint32_t k, float2& acc);
+template <>
+__device__ __forceinline__ void fma_pair16<__nv_bfloat16>(uint32_t q, uint32_t k, float2& acc) {
+  asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\t"
+      "mov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, ql, kl, %0;\n\tfma.rn.f32.bf16 %1, qh, kh, %1;\n\t}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "r"(q), "r"(k));
+}
+template <>
+__device__ __forceinline__ void fma_pair16<__half>(uint32_t q, uint32_t k, float2& acc) {
+  asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\t"
+      "mov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, ql, kl, %0;\n\tfma.rn.f32.f16 %1, qh, kh, %1;\n\t}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "r"(q), "r"(k));
+}
+template <>
+__device__ __forceinline__ void fma_pair16<float>(uint32_t, uint32_t, float2&) {}
+
 // 2^x on the SFU (ex2.approx.ftz.f32); ex2(-inf) = +0.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

@@ -236,16 +236,30 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
 #pragma unroll
     for (int c = 0; c < Tr::kChunks; ++c) {
       const uint32_t kaddr = kslot + k_lane_off + (c >> 3) * 2048 + ((((c & 7) ^ (kr & 7))) << 4);
-      float kf[Tr::kVec];
-      unpack16<T>(lds_v4(kaddr), kf);
+      if constexpr (Tr::kEsize == 2) {
+        // 16-bit q and k feed mixed-precision FMAs as they are (no unpacking);
+        // element e accumulates into sp[r][(e / 2) & 1].x / .y, as the fp32 branch.
+        const uint4 k4 = lds_v4(kaddr);
+        const uint32_t kw[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
-      for (int r = 0; r < NREP; ++r) {
-        float qf[Tr::kVec];  // one broadcast 16-byte read per head and chunk
-        unpack16<T>(lds_v4(qs_addr + (r * D + c * Tr::kVec) * Tr::kEsize), qf);
+        for (int r = 0; r < NREP; ++r) {
+          const uint4 q4 = lds_v4(qs_addr + (r * D + c * Tr::kVec) * Tr::kEsize);  // broadcast
+          const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-        for (int e = 0; e < Tr::kVec; e += 4) {
-          sp[r][0] = __ffma2_rn(make_float2(qf[e + 0], qf[e + 1]), make_float2(kf[e + 0], kf[e + 1]), sp[r][0]);
-          sp[r][1] = __ffma2_rn(make_float2(qf[e + 2], qf[e + 3]), make_float2(kf[e + 2], kf[e + 3]), sp[r][1]);
+          for (int i = 0; i < 4; ++i) fma_pair16<T>(qw[i], kw[i], sp[r][i & 1]);
+        }
+      } else {
+        float kf[Tr::kVec];
+        unpack16<T>(lds_v4(kaddr), kf);
+#pragma unroll
+        for (int r = 0; r < NREP; ++r) {
+          float qf[Tr::kVec];  // one broadcast 16-byte read per head and chunk
+          unpack16<T>(lds_v4(qs_addr + (r * D + c * Tr::kVec) * Tr::kEsize), qf);
+#pragma unroll
+          for (int e = 0; e < Tr::kVec; e += 4) {
+            sp[r][0] = __ffma2_rn(make_float2(qf[e + 0], qf[e + 1]), make_float2(kf[e + 0], kf[e + 1]), sp[r][0]);
+            sp[r][1] = __ffma2_rn(make_float2(qf[e + 2], qf[e + 3]), make_float2(kf[e + 2], kf[e + 3]), sp[r][1]);
+          }
         }
       }
     }
