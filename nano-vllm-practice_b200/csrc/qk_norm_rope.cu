@@ -20,10 +20,14 @@
 // buffers).  Arithmetic is fp32 from the loaded values to the single rounding
 // of the result.
 //
-// Layout: a row is D contiguous elements = D * sizeof(T) / 16 lanes, each
-// holding one 16-byte vector.  The row's sum of squares is reduced over
-// those lanes by xor shuffles, and the rotary partner half (d +- D/2) lives
-// in the lane half a row away, one more xor shuffle.  HBM-bound:
+// Layout: a row is D contiguous elements = D * sizeof(T) / 16 lanes.  Lane
+// `sub` holds 8 bytes of the lower half of the row (dims sub*E/2 ...) and the
+// matching 8 bytes of the upper half (dims D/2 + sub*E/2 ...), so each rotary
+// pair (d, d + D/2) sits in one thread and needs no shuffle; only the row's
+// sum of squares is reduced over the lanes by xor shuffles.  (One 16-byte
+// vector per lane with the partner a shuffle away measured ~10 % slower.)
+// Row loads and stores stay coalesced: the lanes of a row cover each half's
+// bytes contiguously.  HBM-bound:
 // (Hq + 2 Hkv) D sizeof(T) bytes read and written per token, plus 12 bytes
 // of position / slot and the cos / sin rows (L2-resident).  The arithmetic is
 // in packed fp32x2 (FFMA2 / FMUL2) to keep the issue rate below the memory rate.
@@ -61,6 +65,21 @@ __device__ __forceinline__ uint4 pack16<__half>(const float* in) {
 }
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// Rotary pairs in one thread: 8 bytes from the lower half of a row and the matching 8 bytes of the
+// upper half, as one uint4 (.x .y lower, .z .w upper).
+template <typename T, int D>
+__device__ __forceinline__ uint4 ldg_pair(const T* row, int sub) {
+  constexpr int H = 8 / int(sizeof(T));
+  const uint2 lo = __ldg(reinterpret_cast<const uint2*>(row + sub * H));
+  const uint2 hi = __ldg(reinterpret_cast<const uint2*>(row + D / 2 + sub * H));
+  return make_uint4(lo.x, lo.y, hi.x, hi.y);
+}
+template <typename T, int D>
+__device__ __forceinline__ void st_pair(T* row, int sub, const uint4& v) {
+  constexpr int H = 8 / int(sizeof(T));
+  *reinterpret_cast<uint2*>(row + sub * H) = make_uint2(v.x, v.y);
+  *reinterpret_cast<uint2*>(row + D / 2 + sub * H) = make_uint2(v.z, v.w);
+}
 
 constexpr int kThreads = 256;
 
@@ -82,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
     int64_t num_slots, int block_size, int* __restrict__ err) {
   constexpr int E = 16 / int(sizeof(T));  // elements per lane
   constexpr int L = D / E;                // lanes per row
-  constexpr int HALF = L / 2;             // lane distance of the rotary partner
+  constexpr int HALF = L / 2;             // first xor distance of the row reduction
   constexpr int S = kThreads / L;         // row slots per block
   static_assert(L >= 2 && L <= 32 && 32 % L == 0, "row must tile a warp");
   static_assert(E % 2 == 0, "pairs of elements");
@@ -97,14 +116,14 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
   const int u0 = packed ? j % units : j;
   const int ustep = packed ? units : S;  // next head of this slot (one past the end when packed)
   const uint32_t gmask = L == 32 ? 0xffffffffu : (((1u << L) - 1u) << (lane & ~(L - 1)));
-  // rope(y) = y * cos + partner(y) * (+-sin): the sign is fixed per lane.
-  const float sgn = sub < HALF ? -1.f : 1.f;
-  const float2 sgn2 = make_float2(sgn, sgn);
   const float inv_d = 1.f / float(D);
-  const uint4 wq = ldg16(q_w + sub * E), wk = ldg16(k_w + sub * E);  // unpacked where used
+  const uint4 wq = ldg_pair<T, D>(q_w, sub), wk = ldg_pair<T, D>(k_w, sub);  // unpacked where used
 
   // Norm + rope of one q or k row held as raw[] (row-group uniform).
-  auto norm_rope = [&](const uint4& raw, const uint4& wv, const float* c, const float* sn) -> uint4 {
+  auto norm_rope = [&](const uint4& raw, const uint4& wv, const uint4& cr, const uint4& sr) -> uint4 {
+    float c[E], sn[E];
+    unpack16<T>(cr, c);
+    unpack16<T>(sr, sn);
     float x[E], w[E];
     unpack16<T>(raw, x);
     unpack16<T>(wv, w);
@@ -126,21 +145,25 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
       y[e] = yy.x;
       y[e + 1] = yy.y;
     }
+    // y[e] (e < E/2) is dim d of the lower half and y[e + E/2] dim d + D/2: the partner is local.
     float r[E];
 #pragma unroll
-    for (int e = 0; e < E; e += 2) {
-      const float2 yp = make_float2(__shfl_xor_sync(gmask, y[e], HALF), __shfl_xor_sync(gmask, y[e + 1], HALF));
-      const float2 rr = __ffma2_rn(make_float2(y[e], y[e + 1]), make_float2(c[e], c[e + 1]),
-                                   __fmul2_rn(yp, make_float2(sn[e], sn[e + 1])));
-      r[e] = rr.x;
-      r[e + 1] = rr.y;
+    for (int e = 0; e < E / 2; e += 2) {
+      const float2 ylo = make_float2(y[e], y[e + 1]), yhi = make_float2(y[e + E / 2], y[e + E / 2 + 1]);
+      const float2 lo = __ffma2_rn(ylo, make_float2(c[e], c[e + 1]), __fmul2_rn(yhi, make_float2(-sn[e], -sn[e + 1])));
+      const float2 hi = __ffma2_rn(yhi, make_float2(c[e + E / 2], c[e + E / 2 + 1]),
+                                   __fmul2_rn(ylo, make_float2(sn[e + E / 2], sn[e + E / 2 + 1])));
+      r[e] = lo.x;
+      r[e + 1] = lo.y;
+      r[e + E / 2] = hi.x;
+      r[e + E / 2 + 1] = hi.y;
     }
     return pack16<T>(r);
   };
 
   auto load_row = [&](int t, int uu) -> uint4 {
-    if (uu < n_heads) return ldg16(q + int64_t(t) * q_ts + uu * q_hs + sub * E);
-    if (uu < n_heads + n_kv_heads) return ldg16(k + int64_t(t) * k_ts + (uu - n_heads) * k_hs + sub * E);
+    if (uu < n_heads) return ldg_pair<T, D>(q + int64_t(t) * q_ts + uu * q_hs, sub);
+    if (uu < n_heads + n_kv_heads) return ldg_pair<T, D>(k + int64_t(t) * k_ts + (uu - n_heads) * k_hs, sub);
     return ldg16(v + int64_t(t) * v_ts + (uu - n_heads - n_kv_heads) * v_hs + sub * E);
   };
   const int tstride = gridDim.x * tpb;
@@ -160,16 +183,10 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
       slot_n = __ldg(slot_mapping + t + tstride);
     }
     const bool rope_ok = pos >= 0 && pos < rope_rows;
-    float c[E], sn[E];
+    uint4 c = make_uint4(0, 0, 0, 0), sn = make_uint4(0, 0, 0, 0);
     if (rope_ok) {
-      unpack16<T>(ldg16(cos_t + int64_t(pos) * D + sub * E), c);
-      unpack16<T>(ldg16(sin_t + int64_t(pos) * D + sub * E), sn);
-#pragma unroll
-      for (int e = 0; e < E; e += 2) {
-        const float2 s2 = __fmul2_rn(make_float2(sn[e], sn[e + 1]), sgn2);
-        sn[e] = s2.x;
-        sn[e + 1] = s2.y;
-      }
+      c = ldg_pair<T, D>(cos_t + int64_t(pos) * D, sub);
+      sn = ldg_pair<T, D>(sin_t + int64_t(pos) * D, sub);
     }
     if (slot >= num_slots) {
       if (sub == 0) record_error(err, FVB_ERR_BAD_SLOT, t);
@@ -180,12 +197,11 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
     const int off = slot >= 0 ? int(slot - blk * block_size) : 0;
     auto finish = [&](int uu, const uint4& raw) {
       if (uu < n_heads) {
-        if (rope_ok)
-          *reinterpret_cast<uint4*>(q_out + (int64_t(uu) * num_tokens + t) * D + sub * E) = norm_rope(raw, wq, c, sn);
+        if (rope_ok) st_pair<T, D>(q_out + (int64_t(uu) * num_tokens + t) * D, sub, norm_rope(raw, wq, c, sn));
       } else if (uu < n_heads + n_kv_heads) {
         if (rope_ok && slot >= 0)
-          *reinterpret_cast<uint4*>(k_pool + ((blk * n_kv_heads + (uu - n_heads)) * block_size + off) * D + sub * E) =
-              norm_rope(raw, wk, c, sn);
+          st_pair<T, D>(k_pool + ((blk * n_kv_heads + (uu - n_heads)) * block_size + off) * D, sub,
+                        norm_rope(raw, wk, c, sn));
       } else if (slot >= 0) {  // value row: bit-exact copy
         *reinterpret_cast<uint4*>(v_pool + ((blk * n_kv_heads + (uu - n_heads - n_kv_heads)) * block_size + off) * D +
                                   sub * E) = raw;
