@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
     float eps, const T* __restrict__ cos_t, const T* __restrict__ sin_t, int rope_rows,
     const int32_t* __restrict__ positions, const int64_t* __restrict__ slot_mapping, int num_tokens,
     int n_heads, int n_kv_heads, T* __restrict__ q_out, T* __restrict__ k_pool, T* __restrict__ v_pool,
-    int64_t num_slots, int block_size, int* __restrict__ err) {
+    int64_t num_slots, int block_size, int block_shift, int* __restrict__ err) {
   constexpr int E = 16 / int(sizeof(T));  // elements per lane
   constexpr int L = D / E;                // lanes per row
   constexpr int HALF = L / 2;             // first xor distance of the row reduction
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
       slot = -1;
     }
     if (!rope_ok && u0 == 0 && sub == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, t);
-    const int64_t blk = slot >= 0 ? slot / block_size : 0;
+    const int64_t blk = slot < 0 ? 0 : block_shift >= 0 ? (slot >> block_shift) : slot / block_size;
     const int off = slot >= 0 ? int(slot - blk * block_size) : 0;
     auto finish = [&](int uu, const uint4& raw) {
       if (uu < n_heads) {
@@ -234,12 +234,15 @@ cudaError_t launch_typed(const void* q, int64_t q_ts, int64_t q_hs, const void* 
   int64_t blocks = (num_tokens + tpb - 1) / tpb;
   const int64_t cap = int64_t(device_sm_count()) * 3 * 8;  // 8 waves of 3 resident CTAs per SM, then token-stride
   if (blocks > cap) blocks = cap;
+  int block_shift = -1;  // page size a power of two: slot / block_size as a shift
+  for (int b = 0; b < 31; ++b)
+    if ((1 << b) == block_size) block_shift = b;
   qk_norm_rope_store_kernel<T, D><<<unsigned(blocks), kThreads, 0, stream>>>(
       static_cast<const T*>(q), q_ts, q_hs, static_cast<const T*>(k), k_ts, k_hs, static_cast<const T*>(v), v_ts,
       v_hs, static_cast<const T*>(q_w), static_cast<const T*>(k_w), eps, static_cast<const T*>(cos_t),
       static_cast<const T*>(sin_t), rope_rows, positions, slot_mapping, int(num_tokens), n_heads, n_kv_heads,
       static_cast<T*>(q_out), static_cast<T*>(k_pool), static_cast<T*>(v_pool), num_blocks * block_size, block_size,
-      err);
+      block_shift, err);
   return cudaGetLastError();
 }
 
