@@ -21,6 +21,13 @@
 //               the log2 domain, then lane l accumulates p * V for head dims
 //               [l*D/32, (l+1)*D/32) over the stage's tokens.
 //
+// Arithmetic: with 16-bit K/V the q.k products use sm_100's mixed-precision
+// FMA (fma.rn.f32.bf16 / .f16), which takes the 16-bit halves as loaded, and
+// p * V runs on packed fp32x2 FMAs; both give exactly the fp32 FMA results of
+// the unpacked form, in fewer issue slots (the kernel is HBM-bound only once
+// the issue rate stays below the memory rate, which at 4 query heads per kv
+// head it did not before).
+//
 // At the end the four warps' (max, sum, acc) are merged in shared memory; a
 // sequence with a single split writes its output directly, otherwise the
 // normalised partial and its log-sum-exp go to the workspace and
@@ -314,8 +321,19 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
       }
 #pragma unroll
       for (int r = 0; r < NREP; ++r) {
+        if constexpr (Tr::kDPL % 2 == 0) {
+          // packed fp32x2 FMAs over dimension pairs: the same per-element FMA, half the issues
 #pragma unroll
-        for (int i = 0; i < Tr::kDPL; ++i) acc[r][i] = fmaf(pr[r], vf[i], acc[r][i]);
+          for (int i = 0; i < Tr::kDPL; i += 2) {
+            const float2 a = __ffma2_rn(make_float2(pr[r], pr[r]), make_float2(vf[i], vf[i + 1]),
+                                        make_float2(acc[r][i], acc[r][i + 1]));
+            acc[r][i] = a.x;
+            acc[r][i + 1] = a.y;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < Tr::kDPL; ++i) acc[r][i] = fmaf(pr[r], vf[i], acc[r][i]);
+        }
       }
     }
     __syncwarp();
