@@ -148,6 +148,27 @@ def test_store_kvcache_sweep_bit_exact(dtype, cuda_device):
     assert torch.equal(kp.cpu(), kref) and torch.equal(vp.cpu(), vref)
 
 
+@pytest.mark.parametrize("page", [8, 12, 32])
+def test_store_kvcache_other_page_sizes_bit_exact(page, cuda_device):
+    """The write accepts any page size: powers of two split the slot by a shift, others by a division."""
+    T, hkv, d = 300, 4, 128
+    g = torch.Generator().manual_seed(page)
+    k = torch.randn(T, hkv, d, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, hkv, d, generator=g).to(torch.bfloat16)
+    nb = (2 * T + page - 1) // page
+    slots = torch.randperm(nb * page, generator=g)[:T].to(torch.int64)
+    slots[5] = -1
+    kref = torch.zeros(nb, hkv, page, d, dtype=torch.bfloat16)
+    vref = torch.zeros_like(kref)
+    kp, vp = kref.to(cuda_device), vref.to(cuda_device)
+    cabi.store_kvcache(k.to(cuda_device), v.to(cuda_device), kp, vp, slots.to(cuda_device))
+    s = slots.numpy()
+    live = s >= 0
+    kref[s[live] // page, :, s[live] % page] = k[live]
+    vref[s[live] // page, :, s[live] % page] = v[live]
+    assert torch.equal(kp.cpu(), kref) and torch.equal(vp.cpu(), vref)
+
+
 # ---------------------------------------------------------------------------
 # full-size configurations (sampled oracle checks + size-independent properties)
 # ---------------------------------------------------------------------------

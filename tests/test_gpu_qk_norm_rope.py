@@ -244,3 +244,38 @@ def test_host_side_rejections(cuda_device):
     assert st == 3  # FVB_ERR_MISALIGNED
     with pytest.raises(ValueError):
         ops.qk_norm_rope_store(qm.cpu(), km, km, w, w, 1e-6, cos, cos, pos, pool, pool, slots)
+
+
+@pytest.mark.parametrize("page", [8, 12, 32])
+def test_other_page_sizes_write_the_same_rows(page, cuda_device):
+    """Any page size: each slot's K / V row equals the one written with 16-token pages (powers of
+    two split the slot by a shift, others by a division), and q_out does not depend on it."""
+    T, hq, hkv, d = 200, 8, 4, 128
+    g = torch.Generator().manual_seed(100 + page)
+    x = torch.randn(T, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16).to(cuda_device)
+    q = x[:, : hq * d].view(T, hq, d)
+    k = x[:, hq * d : (hq + hkv) * d].view(T, hkv, d)
+    v = x[:, (hq + hkv) * d :].view(T, hkv, d)
+    q_w = (1 + 0.25 * torch.randn(d, generator=g)).to(torch.bfloat16).to(cuda_device)
+    k_w = (1 + 0.25 * torch.randn(d, generator=g)).to(torch.bfloat16).to(cuda_device)
+    rows = 512
+    inv = 1e-6 ** (torch.arange(0, d, 2, dtype=torch.float32) / d)
+    theta = torch.arange(rows, dtype=torch.float32)[:, None] * inv[None]
+    theta = torch.cat([theta, theta], -1)
+    cos = theta.cos().to(torch.bfloat16).to(cuda_device)
+    sin = theta.sin().to(torch.bfloat16).to(cuda_device)
+    positions = torch.randint(0, rows, (T,), generator=g, dtype=torch.int32).to(cuda_device)
+    cap = 2 * T
+    slots = torch.randperm(cap, generator=g)[:T].to(torch.int64)
+
+    def run(p):
+        nb = (cap + p - 1) // p
+        kp = torch.zeros(nb, hkv, p, d, dtype=torch.bfloat16, device=cuda_device)
+        vp = torch.zeros_like(kp)
+        q_out = cabi.qk_norm_rope_store(q, k, v, q_w, k_w, 1e-6, cos, sin, positions, kp, vp, slots.to(cuda_device))
+        return q_out.cpu(), kp.cpu()[slots // p, :, slots % p], vp.cpu()[slots // p, :, slots % p]
+
+    for a, b in zip(run(16), run(page)):
+        assert torch.equal(a, b)
+    assert torch.equal(run(page)[2], v.cpu())
+
