@@ -119,7 +119,9 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
   const float inv_d = 1.f / float(D);
   const uint4 wq = ldg_pair<T, D>(q_w, sub), wk = ldg_pair<T, D>(k_w, sub);  // unpacked where used
 
-  // Norm + rope of one q or k row held as raw[] (row-group uniform).
+  // Norm + rope of one q or k row piece held as raw (lower / upper half pairs, row-group
+  // uniform).  The weights and the token's cos / sin stay packed until here: fewer live
+  // registers let the row loads of both heads issue early (measured ~5 % faster).
   auto norm_rope = [&](const uint4& raw, const uint4& wv, const uint4& cr, const uint4& sr) -> uint4 {
     float c[E], sn[E];
     unpack16<T>(cr, c);
