@@ -89,7 +89,9 @@ FVB_API int fvb_check_bounded_wait(int site, void* stream);
  * 450-490 PyTorch path), which have no native counterpart in the reference.
  * slot_mapping[t] = block_table[s][pos_t / 16] * 16 + pos_t % 16, int64;
  * -1 skips the token.  k / v: [num_tokens][n_kv_heads][head_dim] with
- * element strides (token_stride, head_stride, 1).  Bit-exact copy.
+ * element strides (token_stride, head_stride, 1).  Bit-exact copy.  The pool
+ * may use any page size block_size > 0 (16 above stands for it); the
+ * attention entry points read pools of 16-token pages only.
  */
 FVB_API int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride,
                       void* k_pool, void* v_pool, int64_t num_blocks, const int64_t* slot_mapping,
