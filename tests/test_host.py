@@ -63,6 +63,8 @@ def test_store_rejects_bad_arguments(lib):
     assert lib.fvb_store_kvcache(16, 16, 256, 128, 16, 16, 10, 16, -1, 2, 128, 16, 1, None) == 1
     assert lib.fvb_store_kvcache(16, 16, 256, 128, 16, 16, 10, 12, 4, 2, 128, 16, 1, None) == 3
     assert lib.fvb_store_kvcache(0, 0, 0, 0, 0, 0, 0, 0, 0, 2, 128, 16, 1, None) == 0  # empty: no-op
+    # any positive page size is a valid write target; zero is not
+    assert lib.fvb_store_kvcache(16, 16, 256, 128, 16, 16, 10, 16, 4, 2, 128, 0, 1, None) == 1
 
 
 def test_prefill_rejects_bad_arguments(lib):
@@ -73,6 +75,9 @@ def test_prefill_rejects_bad_arguments(lib):
     bad = list(args)
     bad[11] = 0  # cu_seqlens null
     assert lib.fvb_paged_attention_prefill(*bad) == 1
+    bad = list(args)
+    bad[8] = 32  # attention reads 16-token pages only
+    assert lib.fvb_paged_attention_prefill(*bad) == 2
 
 
 def _sample_args(**over):
