@@ -15,7 +15,8 @@
  *   kv_lens, positions, cu_seqlens: int32
  *
  * dtype codes: FVB_DTYPE_F32, FVB_DTYPE_BF16, FVB_DTYPE_F16.
- * head_dim: 64 or 128.  n_heads / n_kv_heads (GQA group): 1, 2, 4 or 8.
+ * head_dim: 64 or 128.  n_heads / n_kv_heads (GQA group): any whole group, 1 to 16 and
+ * beyond (tiles hold 1, 2, 4, 8 or 16 heads; groups of 3, 5, 6, 7 pad to the next tile).
  */
 #ifndef FEMTOVLLM_B200_H_
 #define FEMTOVLLM_B200_H_
@@ -237,12 +238,18 @@ FVB_API int fvb_paged_attention_prefill_strided(const void* q, int64_t q_token_s
  * (cudaFree synchronizes the device).  Same arguments and result as
  * fvb_paged_attention_decode minus the workspace: the split partials live in a
  * fixed FVB_DECODE_NOALLOC_SCRATCH_BYTES (32 MiB) array inside the library,
- * which every GPU that loads it holds until the process exits.  A launch whose
- * partials need more is rejected unrun with FVB_ERR_WORKSPACE_TOO_SMALL.  The
- * first call on a device looks up the array's device address; make that call
- * before any stream capture.  All calls on a device share the array (nothing in
- * it needs to start at zero), so calls whose kernels overlap on the GPU race.
- * Allocates nothing.
+ * which a GPU holds from the first call on it until the process exits.  A
+ * launch whose partials need more is rejected unrun with
+ * FVB_ERR_WORKSPACE_TOO_SMALL.  The first call on a device looks up the array's
+ * device address (with CUDA's default lazy module loading, that is also when
+ * the 32 MiB are taken on the device), so make that call before any stream
+ * capture and before the KV pool reserves the rest of HBM: a warm-up call with
+ * num_seqs = 0 does it and runs nothing.  The address is cached per device
+ * ordinal, so it is valid in the runtime's primary context of that device (the
+ * context the CUDA runtime and PyTorch use); a caller that switches to its own
+ * driver-API contexts must not use this entry point.  All calls on a device
+ * share the array (nothing in it needs to start at zero), so calls whose
+ * kernels overlap on the GPU race.  Allocates nothing.
  */
 #define FVB_DECODE_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 FVB_API int fvb_paged_attention_decode_noalloc(const void* q, void* out, const void* k_pool, const void* v_pool,

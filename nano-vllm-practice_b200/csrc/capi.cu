@@ -429,8 +429,8 @@ int fvb_paged_attention_decode_strided(const void* q, int64_t q_token_stride, in
     int* err = device_error_ptr(&e);
     if (!err) return cuda_status(e);
     return cuda_status(launch_tc_decode(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs,
-                                        block_tables, max_blocks_per_seq, kv_lens, dtype, tp, lay, workspace, err,
-                                        static_cast<cudaStream_t>(stream)));
+                                        block_tables, max_blocks_per_seq, kv_lens, max_kv_len, dtype, tp, lay,
+                                        workspace, err, static_cast<cudaStream_t>(stream)));
   }
   const DecodePlan plan = plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, max_kv_len, device_sm_count());
   if (plan.ws_bytes > 0 && (!workspace || workspace_bytes < plan.ws_bytes)) return FVB_ERR_WORKSPACE_TOO_SMALL;

@@ -11,11 +11,15 @@
 // fvb_paged_attention_decode_noalloc takes the same arguments as
 // fvb_paged_attention_decode minus the workspace, and uses instead the fixed
 // array g_decode_scratch below (FVB_DECODE_NOALLOC_SCRATCH_BYTES = 32 MiB),
-// which every GPU that loads this library holds until the process exits.
+// which a GPU holds from the first call on it until the process exits.
 //
 // * Set-up: the first call on a device resolves the array's device address
 //   with cudaGetSymbolAddress (with that device current) and caches it per
-//   device; make that first call before any stream capture.
+//   device ordinal.  Under CUDA's default lazy module loading this lookup is
+//   also what loads the array onto the device, so make that first call before
+//   any stream capture and before the engine reserves the rest of HBM for its
+//   KV pool; a call with num_seqs = 0 does only this.  The cached address
+//   belongs to the device's primary context (the one the runtime API uses).
 // * Limit: a launch whose split plan needs more than 32 MiB of partials is
 //   rejected with FVB_ERR_WORKSPACE_TOO_SMALL before anything runs (e.g. 8
 //   sequences x 32 heads at 128k tokens still fit; 64 such sequences do not).

@@ -105,8 +105,9 @@ struct TcDecodePlan {
 TcDecodePlan plan_tc_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int max_kv_len, int num_sms);
 cudaError_t launch_tc_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                              int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
-                             int max_blocks_per_seq, const int32_t* kv_lens, int dtype, const TcDecodePlan& plan,
-                             const QOLayout& lay, void* workspace, int* err, cudaStream_t stream);
+                             int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
+                             const TcDecodePlan& plan, const QOLayout& lay, void* workspace, int* err,
+                             cudaStream_t stream);
 // Merge split partials (decode.cu): sequences with more than one split of
 // pages_per_split pages; the others were written directly.
 cudaError_t launch_decode_combine(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens,

@@ -182,9 +182,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     const __grid_constant__ CUtensorMap vmap, T* __restrict__ out, int64_t q_len_flatten, int num_seqs,
     int n_kv_heads, int64_t num_blocks, const int32_t* __restrict__ cu_seqlens, const int32_t* __restrict__ order,
     const int32_t* __restrict__ cu_items, const int32_t* __restrict__ block_tables, int max_blocks_per_seq,
-    const int32_t* __restrict__ kv_lens, const int32_t* __restrict__ positions, const QOLayout lay, int group,
-    int chunks, int tiles_per_split, int max_splits, float* __restrict__ ws_o, float* __restrict__ ws_lse,
-    int* __restrict__ err) {
+    const int32_t* __restrict__ kv_lens, int kv_cap, const int32_t* __restrict__ positions, const QOLayout lay,
+    int group, int chunks, int tiles_per_split, int max_splits, float* __restrict__ ws_o,
+    float* __restrict__ ws_lse, int* __restrict__ err) {
   using C = Cfg<D>;
   constexpr int TOK = kTileM / NREP;  // query tokens per tile
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -227,10 +227,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   const int ntq = (q_end - q_begin + TOK - 1) / TOK;
   const int pair = (ntq + 1) / 2 - 1 - (item - __ldg(cu_items + lo));  // last (longest-context) pair first
   const bool has1 = 2 * pair + 1 < ntq;
+  // kv_cap <= the block-table row; in decode mode also <= max_kv_len and the split plan's
+  // reach, so a longer kv_len is reported and clamped, never read past or dropped unseen.
   int kv_len = __ldg(kv_lens + s);
-  if (kv_len > max_blocks_per_seq * kPageSize) {
-    if (threadIdx.x == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, s);
-    kv_len = max_blocks_per_seq * kPageSize;
+  if (kv_len > kv_cap) {
+    if (threadIdx.x == 0 && split == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, s);
+    kv_len = kv_cap;
   }
   int t0[2], t_last[2], p_last[2], nkv[2];
 #pragma unroll
@@ -591,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
 template <typename T, int D, int NREP>
 cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                       int n_kv_heads, int num_seqs, int64_t q_len_flatten, const int32_t* cu_seqlens,
-                      const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
+                      const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens, int kv_cap,
                       const int32_t* positions, const PrefillPlan& plan, const QOLayout& lay, int group,
                       int tiles_per_split, int max_splits, float* ws_o, float* ws_lse, void* workspace, int* err,
                       cudaStream_t stream) {
@@ -623,7 +625,7 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   kern<<<unsigned(ctas), kThreads, C::kSmemBytes, stream>>>(qmap, kmap, vmap, static_cast<T*>(out), q_len_flatten,
                                                             num_seqs, n_kv_heads, num_blocks, cu_seqlens, order,
                                                             cu_items, block_tables, max_blocks_per_seq, kv_lens,
-                                                            positions, lay, group, chunks, tiles_per_split,
+                                                            kv_cap, positions, lay, group, chunks, tiles_per_split,
                                                             max_splits, ws_o, ws_lse, err);
   return cudaGetLastError();
 }
@@ -632,12 +634,12 @@ template <typename T, int D>
 cudaError_t dispatch_tc(int nrep, const void* q, void* out, const void* k_pool, const void* v_pool,
                         int64_t num_blocks, int n_kv_heads, int num_seqs, int64_t q_len_flatten,
                         const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
-                        const int32_t* kv_lens, const int32_t* positions, const PrefillPlan& plan,
+                        const int32_t* kv_lens, int kv_cap, const int32_t* positions, const PrefillPlan& plan,
                         const QOLayout& lay, int tiles_per_split, int max_splits, float* ws_o, float* ws_lse, void* ws,
                         int* err, cudaStream_t stream) {
 #define FVB_TC_ARGS q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, block_tables, \
-                    max_blocks_per_seq, kv_lens, positions, plan, lay, nrep, tiles_per_split, max_splits, ws_o,    \
-                    ws_lse, ws, err, stream
+                    max_blocks_per_seq, kv_lens, kv_cap, positions, plan, lay, nrep, tiles_per_split, max_splits,  \
+                    ws_o, ws_lse, ws, err, stream
   switch (tc_tile_heads(nrep)) {
     case 1:
       return launch_tc<T, D, 1>(FVB_TC_ARGS);
@@ -683,9 +685,10 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
   (void)max_q_len;
   if (num_seqs == 0 || q_len_flatten == 0) return cudaSuccess;
   const int nrep = n_heads / n_kv_heads;
+  const int kv_cap = int(std::min<int64_t>(int64_t(max_blocks_per_seq) * kPageSize, 0x7fffffff));
 #define FVB_DISPATCH_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, \
-                          block_tables, max_blocks_per_seq, kv_lens, positions, plan, lay, 0, 1, nullptr, nullptr, \
-                          workspace, err, stream
+                          block_tables, max_blocks_per_seq, kv_lens, kv_cap, positions, plan, lay, 0, 1, nullptr,  \
+                          nullptr, workspace, err, stream
   if (dtype == FVB_DTYPE_BF16) {
     return head_dim == 128 ? dispatch_tc<__nv_bfloat16, 128>(FVB_DISPATCH_ARGS)
                            : dispatch_tc<__nv_bfloat16, 64>(FVB_DISPATCH_ARGS);
@@ -724,10 +727,17 @@ TcDecodePlan plan_tc_decode(int num_seqs, int n_heads, int n_kv_heads, int head_
 
 cudaError_t launch_tc_decode(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                              int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
-                             int max_blocks_per_seq, const int32_t* kv_lens, int dtype, const TcDecodePlan& plan,
-                             const QOLayout& lay, void* workspace, int* err, cudaStream_t stream) {
+                             int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
+                             const TcDecodePlan& plan, const QOLayout& lay, void* workspace, int* err,
+                             cudaStream_t stream) {
   if (num_seqs == 0) return cudaSuccess;
   const int nrep = n_heads / n_kv_heads;
+  // The longest context any sequence may attend over: max_kv_len, the block-table row and,
+  // with split-KV, the splits the plan launches (the combine sizes its shared memory and
+  // reads its partial rows by the same bound).
+  int64_t cap = std::min<int64_t>(max_kv_len, int64_t(max_blocks_per_seq) * kPageSize);
+  if (plan.tiles_per_split > 0) cap = std::min<int64_t>(cap, int64_t(plan.max_splits) * plan.tiles_per_split * kTileN);
+  const int kv_cap = int(cap);
   float* ws_o = nullptr;
   float* ws_lse = nullptr;
   if (plan.tiles_per_split > 0) {
@@ -736,8 +746,8 @@ cudaError_t launch_tc_decode(const void* q, void* out, const void* k_pool, const
   }
   // decode mode: no cu_seqlens / positions (token s = sequence s at position kv_len - 1)
 #define FVB_TCD_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, int64_t(num_seqs), nullptr, \
-                     block_tables, max_blocks_per_seq, kv_lens, nullptr, plan.base, lay, plan.tiles_per_split,    \
-                     plan.max_splits, ws_o, ws_lse, workspace, err, stream
+                     block_tables, max_blocks_per_seq, kv_lens, kv_cap, nullptr, plan.base, lay,                  \
+                     plan.tiles_per_split, plan.max_splits, ws_o, ws_lse, workspace, err, stream
   cudaError_t ce;
   if (dtype == FVB_DTYPE_BF16) {
     ce = head_dim == 128 ? dispatch_tc<__nv_bfloat16, 128>(FVB_TCD_ARGS) : dispatch_tc<__nv_bfloat16, 64>(FVB_TCD_ARGS);
@@ -746,7 +756,7 @@ cudaError_t launch_tc_decode(const void* q, void* out, const void* k_pool, const
   }
 #undef FVB_TCD_ARGS
   if (ce != cudaSuccess || plan.tiles_per_split == 0) return ce;
-  return launch_decode_combine(ws_o, ws_lse, out, kv_lens, max_blocks_per_seq * kPageSize, num_seqs, n_heads,
+  return launch_decode_combine(ws_o, ws_lse, out, kv_lens, kv_cap, num_seqs, n_heads,
                                head_dim, plan.tiles_per_split * (kTileN / kPageSize), plan.max_splits, dtype, lay,
                                stream);
 }

@@ -11,6 +11,7 @@ import torch
 
 import cabi
 import oracle
+import torch_ref
 from conftest import GOLDEN_CASES, golden_after, load_golden
 from femtovllm_b200 import workloads
 
@@ -182,6 +183,31 @@ def _sample(b, n=6, seed=0):
     return sorted(pick)
 
 
+def _check_every_row(out, b, md, what, seqs, decode):
+    """Every output row against the fp32 device restatement (tests/torch_ref.py), which is
+    itself pinned to the numpy oracle on `seqs` first."""
+    ref = torch_ref.paged_attention_fp32(b.q, b.k_pool, b.v_pool, None if decode else md["cu_seqlens"],
+                                         md["block_tables"], md["kv_lens"], None if decode else md["positions"])
+    sub = workloads.subset_for_oracle(b, seqs)
+    if decode:
+        pin = oracle.decode_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["block_tables"], sub["kv_lens"])
+    else:
+        pin = oracle.prefill_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["cu_seqlens"],
+                                       sub["block_tables"], sub["kv_lens"], sub["positions"])
+    tok = torch.from_numpy(sub["tokens"]).to(out.device)
+    pin_err = np.abs(ref[:, tok].cpu().numpy() - pin).max()
+    assert pin_err <= 1e-5, f"{what}: device restatement differs from the oracle by {pin_err:.3g}"
+    assert_close(out[:, tok], pin, b.dtype, f"{what} (oracle sample)")
+    got = out.float()
+    assert torch.isfinite(got).all(), f"{what}: non-finite output"
+    err = (got - ref).abs()
+    max_tol, mean_tol = TOL[b.dtype]
+    worst = int(err.amax(dim=(0, 2)).argmax())
+    assert err.max().item() <= max_tol, f"{what}: max abs {err.max().item():.3g} (token {worst}) > {max_tol}"
+    assert err.mean().item() <= mean_tol, f"{what}: mean abs {err.mean().item():.3g} > {mean_tol}"
+    return ref
+
+
 def test_config2_decode_full_size(cuda_device):
     b = workloads.config2().materialize(cuda_device)
     md = b.device_metadata(cuda_device)
@@ -189,27 +215,34 @@ def test_config2_decode_full_size(cuda_device):
     out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
     out2 = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
     assert torch.equal(out, out2), "decode is not deterministic"
-    seqs = _sample(b)
-    sub = workloads.subset_for_oracle(b, seqs)
-    ref = oracle.decode_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["block_tables"], sub["kv_lens"],
-                                  acc_dtype=np.float32)
-    assert_close(out[:, seqs], ref, torch.bfloat16, "config2")
+    _check_every_row(out, b, md, "config2", _sample(b), decode=True)
     # the new token is visible: its slot now holds k_new
+    seqs = _sample(b)
     s = b.slot_mapping[seqs[0]]
     assert torch.equal(b.k_pool[s // 16, :, s % 16], b.k_new[seqs[0]])
     assert cabi.read_device_error() == (0, 0)
 
 
-def test_config5_long_decode_sample(cuda_device):
-    lens = np.array([32768, 131072, 77777, 40001], dtype=np.int32)
-    b = workloads.custom(lens, np.ones(4), 32, 8, 128, torch.bfloat16, seed=55, pool_factor=1.05).materialize(cuda_device)
+@pytest.mark.parametrize("world,rank", [(1, 0), (4, 3), (8, 0), (8, 7)])
+def test_config5_long_decode_shard_every_row(world, rank, cuda_device):
+    """The rank's LPT shard of config 5 exactly as `bench.py` runs it (own pool, own tables)."""
+    b = workloads.config5(rank=rank, world=world).materialize(cuda_device)
     md = b.device_metadata(cuda_device)
     out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
-    for s in (0, 1):
-        sub = workloads.subset_for_oracle(b, [s])
-        ref = oracle.decode_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["block_tables"], sub["kv_lens"],
-                                      acc_dtype=np.float32)
-        assert_close(out[:, [s]], ref, torch.bfloat16, f"long decode seq {s}")
+    _check_every_row(out, b, md, f"config5 rank {rank} of {world}", [int(np.argmax(b.kv_lens))], decode=True)
+    assert cabi.read_device_error() == (0, 0)
+
+
+@pytest.mark.parametrize("n_heads,n_seqs", [(64, 16), (128, 4)])
+def test_tensor_core_decode_split_every_row(n_heads, n_seqs, cuda_device):
+    """GQA 8 / 16 decode on the tcgen05 route with split-KV (few long sequences)."""
+    lens = np.random.default_rng(n_heads).integers(32768, 131073, size=n_seqs)
+    b = workloads.custom(lens, np.ones(n_seqs), n_heads, 8, 128, torch.bfloat16, seed=n_heads,
+                         pool_factor=1.05).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
+    _check_every_row(out, b, md, f"tc decode GQA {n_heads // 8}", [int(np.argmin(b.kv_lens))], decode=True)
+    assert cabi.read_device_error() == (0, 0)
 
 
 def test_config3_prefill_full_size(cuda_device):
@@ -217,12 +250,8 @@ def test_config3_prefill_full_size(cuda_device):
     md = b.device_metadata(cuda_device)
     out = cabi.prefill(b.q, b.k_pool, b.v_pool, md["cu_seqlens"], b.max_q_len, md["block_tables"], md["kv_lens"],
                        md["positions"])
-    # two sequences against the oracle: the shortest total and one random
-    seqs = [int(np.argmin(b.kv_lens)), 7]
-    sub = workloads.subset_for_oracle(b, seqs)
-    ref = oracle.prefill_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["cu_seqlens"], sub["block_tables"],
-                                   sub["kv_lens"], sub["positions"], acc_dtype=np.float32)
-    assert_close(out[:, torch.from_numpy(sub["tokens"]).to(cuda_device)], ref, torch.bfloat16, "config3")
+    _check_every_row(out, b, md, "config3", [int(np.argmin(b.kv_lens)), 7], decode=False)
+    assert cabi.read_device_error() == (0, 0)
 
 
 def test_config4_mixed_full_size(cuda_device):
@@ -232,17 +261,16 @@ def test_config4_mixed_full_size(cuda_device):
                        md["positions"])
     dec = [int(i) for i in np.nonzero(b.q_lens == 1)[0][:3]]
     pre = [int(np.nonzero(b.q_lens > 1)[0][0])]
-    sub = workloads.subset_for_oracle(b, dec + pre)
-    ref = oracle.prefill_attention(sub["q"], sub["k_pool"], sub["v_pool"], sub["cu_seqlens"], sub["block_tables"],
-                                   sub["kv_lens"], sub["positions"], acc_dtype=np.float32)
-    assert_close(out[:, torch.from_numpy(sub["tokens"]).to(cuda_device)], ref, torch.bfloat16, "config4")
+    _check_every_row(out, b, md, "config4", dec + pre, decode=False)
     # decode rows through the decode kernel agree with the unified launch
     dmask = b.q_lens == 1
     tok = torch.from_numpy(b.cu_seqlens[:-1][dmask].astype(np.int64)).to(cuda_device)
     tabs = md["block_tables"][torch.from_numpy(np.nonzero(dmask)[0]).to(cuda_device)].contiguous()
     lens = md["kv_lens"][torch.from_numpy(np.nonzero(dmask)[0]).to(cuda_device)].contiguous()
     dout = cabi.decode(b.q[:, tok].contiguous(), b.k_pool, b.v_pool, tabs, lens, int(b.kv_lens[dmask].max()))
-    assert (dout.float() - out[:, tok].float()).abs().max().item() <= 2e-2
+    diff = (dout.float() - out[:, tok].float()).abs()
+    assert diff.max().item() <= 2e-2 and diff.mean().item() <= 2e-3, (diff.max().item(), diff.mean().item())
+    assert cabi.read_device_error() == (0, 0)
 
 
 # ---------------------------------------------------------------------------
@@ -276,6 +304,23 @@ def test_kv_len_beyond_max_kv_len_is_clamped_and_reported(cuda_device):
     cabi.read_device_error()
     cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], 32)  # max_kv_len < kv_lens[0]
     assert cabi.read_device_error()[0] == 1
+
+
+@pytest.mark.parametrize("lens,max_kv", [([3000, 200, 5000], 4000), ([300, 900, 40], 512)])
+def test_tensor_core_decode_clamps_kv_len_to_max_kv_len(lens, max_kv, cuda_device):
+    """GQA 8 (tcgen05 route, split-KV for these few sequences): a kv_len above max_kv_len is
+    reported and attends over the first max_kv_len keys, like the SIMT route."""
+    b = workloads.custom(lens, np.ones(len(lens)), 64, 8, 128, torch.bfloat16, seed=4).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    cabi.read_device_error()
+    out = cabi.decode(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], max_kv)
+    code, info = cabi.read_device_error()
+    assert code == 1 and b.kv_lens[info] > max_kv
+    clamped = torch.clamp(md["kv_lens"], max=max_kv)
+    ref = torch_ref.paged_attention_fp32(b.q, b.k_pool, b.v_pool, None, md["block_tables"], clamped)
+    assert torch.isfinite(out.float()).all()
+    err = (out.float() - ref).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, (err.max().item(), err.mean().item())
 
 
 # ---------------------------------------------------------------------------

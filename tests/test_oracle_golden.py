@@ -44,6 +44,24 @@ def test_attention_matches_reference(name):
 
 
 @pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_torch_restatement_matches_reference(name):
+    """tests/torch_ref.py (the full-row checker of the GPU tests) on the reference's own outputs."""
+    import torch
+
+    import torch_ref
+
+    d = load_golden(name)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    kp, vp = t(golden_after(d, "k")), t(golden_after(d, "v"))
+    out = torch_ref.paged_attention_fp32(t(d["q"]), kp, vp, t(d["cu_seqlens"]), t(d["block_tables"]),
+                                         t(d["kv_lens"]), t(d["positions"]), q_chunk=5)
+    assert np.abs(out.numpy() - d["out_ref"]).max() < 2e-5
+    if d["is_decode"]:
+        dec = torch_ref.paged_attention_fp32(t(d["q"]), kp, vp, None, t(d["block_tables"]), t(d["kv_lens"]))
+        assert np.abs(dec.numpy() - d["out_ref"]).max() < 2e-5
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
 def test_decode_and_prefill_forms_agree(name):
     d = load_golden(name)
     if not d["is_decode"]:

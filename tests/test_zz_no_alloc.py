@@ -45,16 +45,19 @@ def decode_noalloc(q, k_pool, v_pool, tables, kv_lens, max_kv_len):
     return st, out
 
 
-def _close(a, b, dtype):
-    err = (a.float() - b.float()).abs()
-    max_tol, mean_tol = (1e-4, 1e-4) if dtype == torch.float32 else (2e-2, 2e-3)
-    assert torch.isfinite(a.float()).all()
-    assert err.max().item() <= max_tol and err.mean().item() <= mean_tol, (err.max().item(), err.mean().item())
+# config 2 / config 1: the SIMT split-KV route; the GQA-8 case of few long sequences: the
+# tcgen05 route with split-KV, whose tile plan and partials both live in the scratch array.
+CASES = {
+    "config2_bf16_gqa2": lambda: workloads.config2(),
+    "config1_fp32_gqa4": lambda: workloads.config1(),
+    "gqa8_bf16_tensor_core_split": lambda: workloads.custom([8192, 7000, 8100, 6001], [1, 1, 1, 1], 32, 4, 128,
+                                                            torch.bfloat16, seed=8),
+}
 
 
-@pytest.mark.parametrize("make", [lambda: workloads.config2(), lambda: workloads.config1()])
-def test_noalloc_matches_workspace_entry_point_on_two_calls(make, cuda_device):
-    b = make().materialize(cuda_device)
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_noalloc_matches_workspace_entry_point_on_two_calls(case, cuda_device):
+    b = CASES[case]().materialize(cuda_device)
     md = b.device_metadata(cuda_device)
     ws_bytes = cabi.lib().fvb_paged_attention_decode_workspace_size(b.num_seqs, b.n_heads, b.n_kv_heads, b.head_dim,
                                                                     b.max_kv_len)
@@ -64,8 +67,20 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(make, cuda_device):
         st, out = decode_noalloc(b.q, b.k_pool, b.v_pool, md["block_tables"], md["kv_lens"], b.max_kv_len)
         assert st == 0, capi.STATUS_NAMES.get(st, st)
         torch.cuda.synchronize()
-        _close(out, ref, b.dtype)
+        # the same plan and kernels run on the same inputs: the outputs are bit-identical
+        assert torch.isfinite(out.float()).all()
+        assert torch.equal(out, ref)
     assert cabi.read_device_error() == (0, 0)
+
+
+def test_noalloc_warm_up_call_with_no_sequences(cuda_device):
+    """num_seqs = 0 resolves the array's address (loading it on the device) and runs nothing."""
+    z = torch.zeros(1, dtype=torch.bfloat16, device=cuda_device)
+    t = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    st = _noalloc_fn()(z.data_ptr(), z.data_ptr(), z.data_ptr(), z.data_ptr(), 1, 8, 2, 128, 16, 0, t.data_ptr(), 1,
+                       t.data_ptr(), 0, capi.dtype_code(torch.bfloat16),
+                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 0
 
 
 def test_noalloc_rejects_a_plan_larger_than_its_scratch(cuda_device):
