@@ -686,11 +686,13 @@ def _r(x, n=5):
 
 
 def _e2e(g, key_units, unit, scale):
+    """End-to-end figure: the median over blocks of K host-pipelined steps (the first block after the
+    warm-up also carries the host's one-time costs; it is reported beside it)."""
     t = max(x["e2e_ms"] for x in g)
     tm = max(x["e2e_ms_median"] for x in g)
     units = sum(x[key_units] for x in g)
-    return {"value": _r(units / (t * 1e-3) / scale, 2), "unit": unit, "ms_per_step": _r(t),
-            "value_median_blocks": _r(units / (tm * 1e-3) / scale, 2),
+    return {"value": _r(units / (tm * 1e-3) / scale, 2), "unit": unit, "ms_per_step": _r(tm),
+            "value_first_block": _r(units / (t * 1e-3) / scale, 2),
             "h2d_bytes_per_step": sum(x["h2d"] for x in g), "d2h_bytes_per_step": sum(x["d2h"] for x in g)}
 
 
@@ -826,10 +828,11 @@ def _line_decode(ctx, d, cpu):
         },
         "cpu_baseline": cpu,
         "e2e": {
-            "value": round(total_bytes / (max(x["e2e_ms"] for x in d) * 1e-3) / 1e9, 2),
+            "value": round(total_bytes / (max(x["e2e_ms_median"] for x in d) * 1e-3) / 1e9, 2),
             "unit": "GB/s",
-            "ms_per_step": round(max(x["e2e_ms"] for x in d), 5),
-            "value_median_blocks": round(total_bytes / (max(x["e2e_ms_median"] for x in d) * 1e-3) / 1e9, 2),
+            "ms_per_step": round(max(x["e2e_ms_median"] for x in d), 5),
+            "value_first_block": round(total_bytes / (max(x["e2e_ms"] for x in d) * 1e-3) / 1e9, 2),
+            "timing": "median over blocks of K end-to-end steps (>= 0.5 s), max over ranks",
             "h2d_bytes_per_step": sum(x["h2d"] for x in d),
             "d2h_bytes_per_step": sum(x["d2h"] for x in d),
             "api": "femtovllm_b200.ops.store_kvcache + paged_attention_gemv from pinned host buffers "

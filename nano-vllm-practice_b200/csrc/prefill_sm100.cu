@@ -108,11 +108,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 // Work plan of one launch (one CTA):
 //  order[p]    = p-th sequence by descending kv_len (identity beyond kSortMaxSeqs
 //                sequences), so the longest-context work is dispatched first;
-//  cu_items[p] = exclusive scan of ceil(ceil(q_len / tile_tokens) / 2) (query-tile
-//                pairs) over that order.
+//  cu_items[p] = exclusive scan of ceil(ceil(q_len / tile_tokens) / tiles_per_item)
+//                (work items of that many query tiles) over that order.
 __global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __restrict__ cu_seqlens,
                                                             const int32_t* __restrict__ kv_lens, int num_seqs,
-                                                            int tile_tokens, int32_t* __restrict__ order,
+                                                            int tile_tokens, int tiles_per_item,
+                                                            int32_t* __restrict__ order,
                                                             int32_t* __restrict__ cu_items) {
   __shared__ int kv_sh[kSortMaxSeqs];
   __shared__ int warp_tot[32];
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __res
       // decode mode (cu_seqlens == nullptr): one query token per sequence
       const int ql = cu_seqlens ? __ldg(cu_seqlens + s + 1) - __ldg(cu_seqlens + s) : 1;
       const int tiles = ql > 0 ? (ql + tile_tokens - 1) / tile_tokens : 0;
-      v = (tiles + 1) / 2;
+      v = (tiles + tiles_per_item - 1) / tiles_per_item;
     }
     int x = v;
 #pragma unroll
@@ -614,8 +615,7 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   if (ce != cudaSuccess) return ce;
   int32_t* order = static_cast<int32_t*>(workspace);
   int32_t* cu_items = order + ((num_seqs + 63) & ~63);
-  prefill_plan_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, kv_lens, num_seqs, TOK, order, cu_items);
-  ce = cudaGetLastError();
+  ce = launch_prefill_plan(cu_seqlens, kv_lens, num_seqs, TOK, 2, order, cu_items, stream);
   if (ce != cudaSuccess) return ce;
   auto kern = prefill_tc_kernel<T, D, NREP>;
   ce = set_smem_once<prefill_tc_kernel<T, D, NREP>>(C::kSmemBytes);
@@ -656,6 +656,13 @@ cudaError_t dispatch_tc(int nrep, const void* q, void* out, const void* k_pool, 
 }
 
 }  // namespace
+
+cudaError_t launch_prefill_plan(const int32_t* cu_seqlens, const int32_t* kv_lens, int num_seqs, int tile_tokens,
+                                int tiles_per_item, int32_t* order, int32_t* cu_items, cudaStream_t stream) {
+  prefill_plan_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, kv_lens, num_seqs, tile_tokens, tiles_per_item, order,
+                                              cu_items);
+  return cudaGetLastError();
+}
 
 PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int64_t q_len_flatten,
                          int max_q_len, int dtype) {
