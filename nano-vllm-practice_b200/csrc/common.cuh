@@ -196,9 +196,11 @@ __device__ __forceinline__ uint32_t cluster_smem_addr(const void* p, uint32_t ra
   return r;
 }
 
-// One arrival (release at cluster scope) on an mbarrier given by its shared::cluster address.
+// One arrival on an mbarrier given by its shared::cluster address (possibly in another CTA of
+// the cluster), with the instruction's default semantics, as CUTLASS's ClusterBarrier does;
+// the data it hands over is ordered by the tcgen05 / proxy fences the callers issue.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // Make initialized mbarriers visible to the other CTAs of the cluster.

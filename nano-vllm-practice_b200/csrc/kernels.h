@@ -98,15 +98,6 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
 cudaError_t launch_prefill_plan(const int32_t* cu_seqlens, const int32_t* kv_lens, int num_seqs, int tile_tokens,
                                 int tiles_per_item, int32_t* order, int32_t* cu_items, cudaStream_t stream);
 
-// Prefill on CTA pairs (prefill_sm100_pair.cu): bf16 / f16, head_dim 128, the same
-// workspace as launch_prefill (the plan: order + cu_items).
-int64_t prefill_pair_max_items(int num_seqs, int n_heads, int n_kv_heads, int64_t q_len_flatten);
-cudaError_t launch_prefill_pair(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
-                                int n_heads, int n_kv_heads, int num_seqs, int64_t q_len_flatten,
-                                const int32_t* cu_seqlens, const int32_t* block_tables, int max_blocks_per_seq,
-                                const int32_t* kv_lens, const int32_t* positions, int dtype, const QOLayout& lay,
-                                void* workspace, int* err, cudaStream_t stream);
-
 // Decode on the tensor-core attention kernel (decode mode: token s of sequence s at
 // position kv_len - 1), with split-KV when there are too few (sequence, kv head) CTAs.
 struct TcDecodePlan {

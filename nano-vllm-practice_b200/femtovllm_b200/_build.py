@@ -58,7 +58,6 @@ CU_SOURCES = [
     "decode_noalloc.cu",
     "prefill_simt.cu",
     "prefill_sm100.cu",
-    "prefill_sm100_pair.cu",
 ]
 
 
