@@ -603,7 +603,7 @@ def block_long_config5(ctx):
     """Config 5's 64 sequences split longest-first over the ranks (strong scaling)."""
     from femtovllm_b200 import ops, workloads
 
-    b = workloads.config5(rank=ctx.rank, world=ctx.world).materialize(ctx.dev)
+    b = workloads.config5(rank=ctx.rank, world=ctx.world, total=ctx.args.long_total).materialize(ctx.dev)
     md = b.device_metadata(ctx.dev)
     tab, lens = md["block_tables"], md["kv_lens"]
 
@@ -869,7 +869,7 @@ def _add_blocks(ctx, line, blocks):
         ach = g[slow]["bytes"] / (g[slow]["ms"] * 1e-3) / 1e9
         line["long_config5"] = {
             "workload": "long_config5", "unit": "tokens/s",
-            "config": {"total_seqs": 64, "n_heads": 32, "n_kv_heads": 8, "head_dim": 128, "kv_len": "U[32768,131072]",
+            "config": {"total_seqs": args.long_total, "n_heads": 32, "n_kv_heads": 8, "head_dim": 128, "kv_len": "U[32768,131072]",
                        "sharding": f"longest-first over {world} rank(s), each with its own pool (strong scaling)",
                        "seqs_per_rank": [x["tokens"] for x in g], "kv_tokens_per_rank": [x["kv_tokens"] for x in g]},
             "value": _r(toks / (t * 1e-3), 1), "ms_per_step": _r(t),
@@ -1092,6 +1092,8 @@ def main():
     ap.add_argument("--workload", default="all",
                     choices=["all", "prefill", "mixed", "long", "store", "qk_norm_rope", "decode_graph", "sampler"],
                     help="all = the contract line (config 2 + every block); the others run one measurement alone")
+    ap.add_argument("--long-total", type=int, default=64,
+                    help="config 5's total sequences over all ranks (64; fewer only for profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true", help="skip the reference Triton prefill timing")
     args = ap.parse_args()
