@@ -891,7 +891,7 @@ def _add_blocks(ctx, line, blocks):
             "workload": "store_kvcache of 65,536 tokens per GPU (Hkv 8, D 128, bf16, random slots)", "unit": "GB/s",
             "value": _r(sum(x["bytes"] for x in g) / (t * 1e-3) / 1e9, 1), "ms_per_step": _r(t),
             "sustained_ms_per_step": _r(max(x["ms_median"] for x in g)),
-            "roofline": {"kernel": "store_kvcache_kernel", "bound": "hbm", "achieved": _r(ach, 1), "peak": hbm,
+            "roofline": {"kernel": "store_kvcache_bulk_kernel", "bound": "hbm", "achieved": _r(ach, 1), "peak": hbm,
                          "unit": "GB/s", "frac": _r(ach / hbm, 4), "traffic": _profile_traffic("store_65k")},
             "clocks": g[0]["clocks"], "gpu_launches": args.steps,
         }

@@ -9,6 +9,11 @@
 // group of lanes copies with one coalesced load and one coalesced store each.
 // HBM-bound: 2 * T * Hkv * D * sizeof(T) bytes read and written, plus 8 T
 // bytes of slot_mapping.
+//
+// Two kernels: store_kvcache_bulk_kernel (16-byte-aligned rows, the usual
+// case) moves whole rows with the TMA engine's bulk copies, global -> shared ->
+// global, and store_kvcache_kernel (any alignment) moves them as vectors
+// through registers.
 #include <algorithm>
 
 #include "common.cuh"
@@ -92,6 +97,105 @@ __global__ void __launch_bounds__(256) store_kvcache_kernel(const uint8_t* __res
   }
 }
 
+// Bulk-copy path.  A CTA takes chunks of `tok` tokens (grid-stride): thread 0
+// loads each token's K rows and V rows (n_kv_heads rows each, one bulk copy per
+// token and tensor when a token's heads are contiguous, one per row otherwise)
+// into one of two shared-memory stages, completing on that stage's mbarrier;
+// then every thread stores rows of the chunk (K rows, then V rows, per token)
+// to their pool slots with one bulk store each (cp.async.bulk global <- shared,
+// one bulk group per thread and chunk).  The next chunk's loads go to the other
+// stage as soon as this thread's stores of the chunk before it have been read
+// out of shared memory, so a chunk's loads overlap the previous chunk's stores.
+// Measured at 65,536 tokens of (8 heads x 128 dims, bf16) with random slots:
+// 5.79 TB/s against 4.94 TB/s for the vector kernel (chunks of 4 tokens, 64
+// threads, 4 CTAs per SM; 2, 8 and 16 tokens or 3, 5, 6 and 8 CTAs per SM were
+// slower).
+constexpr int kBulkThreads = 64;
+constexpr int kBulkCtasPerSm = 4;
+constexpr int kBulkStageBytes = 16 * 1024;  // tokens per chunk = this / (bytes of a token's rows), at most 4
+
+__device__ __forceinline__ void bulk_s2g(void* dst_gmem, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem), "r"(src_smem),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's bulk stores have all finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_reads() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's bulk stores have all completed.
+__device__ __forceinline__ void bulk_wait_done() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kBulkThreads) store_kvcache_bulk_kernel(
+    const uint8_t* __restrict__ k, const uint8_t* __restrict__ v, int64_t token_stride_b, int64_t head_stride_b,
+    uint8_t* __restrict__ k_pool, uint8_t* __restrict__ v_pool, int64_t num_slots,
+    const int64_t* __restrict__ slot_mapping, int64_t num_tokens, int n_kv_heads, int row_bytes, int tok,
+    int block_size, int block_shift, int* __restrict__ err) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int R = 2 * n_kv_heads;  // rows per token
+  const int tok_bytes = R * row_bytes;
+  const int stage_bytes = tok * tok_bytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + 2 * stage_bytes);
+  const int tid = threadIdx.x;
+  const bool heads_contiguous = head_stride_b == row_bytes;
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int64_t nchunks = (num_tokens + tok - 1) / tok;
+  auto load_chunk = [&](int64_t c, int st) {  // thread 0
+    const int64_t t0 = c * tok;
+    const int nt = num_tokens - t0 < tok ? int(num_tokens - t0) : tok;
+    mbar_arrive_expect_tx(&bar[st], uint32_t(nt) * uint32_t(tok_bytes));
+    uint8_t* dst = sm + st * stage_bytes;
+    for (int i = 0; i < nt; ++i) {
+      const uint8_t* ks = k + (t0 + i) * token_stride_b;
+      const uint8_t* vs = v + (t0 + i) * token_stride_b;
+      uint8_t* d = dst + i * tok_bytes;
+      if (heads_contiguous) {
+        bulk_g2s(d, ks, uint32_t(n_kv_heads * row_bytes), &bar[st]);
+        bulk_g2s(d + n_kv_heads * row_bytes, vs, uint32_t(n_kv_heads * row_bytes), &bar[st]);
+      } else {
+        for (int h = 0; h < n_kv_heads; ++h) {
+          bulk_g2s(d + h * row_bytes, ks + h * head_stride_b, uint32_t(row_bytes), &bar[st]);
+          bulk_g2s(d + (n_kv_heads + h) * row_bytes, vs + h * head_stride_b, uint32_t(row_bytes), &bar[st]);
+        }
+      }
+    }
+  };
+  int it = 0;
+  if (tid == 0 && int64_t(blockIdx.x) < nchunks) load_chunk(blockIdx.x, 0);
+  for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x, ++it) {
+    const int st = it & 1;
+    bulk_wait_reads();  // the other stage's stores (previous chunk) are out of shared memory
+    __syncthreads();
+    if (tid == 0 && c + gridDim.x < nchunks) load_chunk(c + gridDim.x, st ^ 1);
+    const bool landed = mbar_wait(&bar[st], uint32_t(it >> 1) & 1u, err, 0x500);
+    if (!__syncthreads_and(landed)) break;
+    const int64_t t0 = c * tok;
+    for (int row = tid; row < tok * R; row += kBulkThreads) {
+      const int i = row / R, r = row - i * R;
+      const int64_t t = t0 + i;
+      if (t >= num_tokens) continue;
+      const int64_t slot = __ldg(slot_mapping + t);
+      if (slot >= num_slots) {
+        if (r == 0) record_error(err, FVB_ERR_BAD_SLOT, int(t));
+        continue;
+      }
+      if (slot < 0) continue;  // padding token
+      const int h = r < n_kv_heads ? r : r - n_kv_heads;
+      const int64_t blk = block_shift >= 0 ? (slot >> block_shift) : slot / block_size;
+      const int off = int(slot - blk * block_size);
+      uint8_t* dst = (r < n_kv_heads ? k_pool : v_pool) +
+                     ((blk * n_kv_heads + h) * block_size + off) * int64_t(row_bytes);
+      bulk_s2g(dst, smem_u32(sm + st * stage_bytes + row * row_bytes), uint32_t(row_bytes));
+    }
+    bulk_commit_group();
+  }
+  bulk_wait_done();  // no copy of this CTA is in flight when it exits
+}
+
 cudaError_t launch_store_kvcache(const void* k, const void* v, int64_t token_stride, int64_t head_stride,
                                  void* k_pool, void* v_pool, int64_t num_blocks, const int64_t* slot_mapping,
                                  int64_t num_tokens, int n_kv_heads, int head_dim, int block_size, int esize,
@@ -123,6 +227,19 @@ cudaError_t launch_store_kvcache(const void* k, const void* v, int64_t token_str
   auto* vb = static_cast<const uint8_t*>(v);
   auto* kp = static_cast<uint8_t*>(k_pool);
   auto* vp = static_cast<uint8_t*>(v_pool);
+  const int tok_bytes = 2 * n_kv_heads * row_bytes;
+  if (vec_bytes == 16 && tok_bytes <= kBulkStageBytes) {
+    // Bulk copies need 16-byte-aligned addresses and sizes: every row start and length here is.
+    // tok * tok_bytes <= 16 KB, so the two stages stay under the 48 KB default dynamic shared memory.
+    const int tok = std::min(4, kBulkStageBytes / tok_bytes);
+    const int smem = 2 * tok * tok_bytes + 16;
+    const int64_t nchunks = (num_tokens + tok - 1) / tok;
+    const int64_t grid = std::min<int64_t>(nchunks, int64_t(device_sm_count()) * kBulkCtasPerSm);
+    store_kvcache_bulk_kernel<<<unsigned(grid), kBulkThreads, smem, stream>>>(
+        kb, vb, ts_b, hs_b, kp, vp, num_slots, slot_mapping, num_tokens, n_kv_heads, row_bytes, tok, block_size,
+        block_shift, err);
+    return cudaGetLastError();
+  }
   switch (vec_bytes) {
     case 16:
       store_kvcache_kernel<16><<<unsigned(blocks), threads, 0, stream>>>(kb, vb, ts_b, hs_b, kp, vp, num_slots,
