@@ -149,6 +149,37 @@ def test_store_kvcache_sweep_bit_exact(dtype, cuda_device):
     assert torch.equal(kp.cpu(), kref) and torch.equal(vp.cpu(), vref)
 
 
+@pytest.mark.parametrize("layout", ["head_major_view", "unaligned"])
+def test_store_kvcache_layouts_bit_exact(layout, cuda_device):
+    """Rows whose heads are not adjacent (one bulk copy per row) and rows that are not 16-byte aligned
+    (the vector kernel) write the same pools as the reference loop."""
+    T, hkv, d = 77, 4, 128
+    g = torch.Generator().manual_seed(31)
+    kh = torch.randn(hkv, T, d, generator=g).to(torch.bfloat16)
+    vh = torch.randn(hkv, T, d, generator=g).to(torch.bfloat16)
+    if layout == "head_major_view":  # (T, Hkv, D) view of head-major storage: head stride T * D
+        k, v = kh.to(cuda_device).transpose(0, 1), vh.to(cuda_device).transpose(0, 1)
+    else:  # one element past a 16-byte boundary
+        flat = torch.empty(2 * T * hkv * d + 2, dtype=torch.bfloat16, device=cuda_device)
+        k = flat[1 : 1 + T * hkv * d].view(T, hkv, d)
+        v = flat[1 + T * hkv * d : 1 + 2 * T * hkv * d].view(T, hkv, d)
+        k.copy_(kh.transpose(0, 1))
+        v.copy_(vh.transpose(0, 1))
+    nb = (2 * T + 15) // 16
+    slots = torch.randperm(nb * 16, generator=g)[:T].to(torch.int64)
+    slots[3] = -1
+    kref = torch.zeros(nb, hkv, 16, d, dtype=torch.bfloat16)
+    vref = torch.zeros_like(kref)
+    kp, vp = kref.to(cuda_device), vref.to(cuda_device)
+    cabi.store_kvcache(k, v, kp, vp, slots.to(cuda_device))
+    s = slots.numpy()
+    live = s >= 0
+    kref[s[live] // 16, :, s[live] % 16] = kh.transpose(0, 1)[live]
+    vref[s[live] // 16, :, s[live] % 16] = vh.transpose(0, 1)[live]
+    assert torch.equal(kp.cpu(), kref) and torch.equal(vp.cpu(), vref)
+    assert cabi.read_device_error() == (0, 0)
+
+
 @pytest.mark.parametrize("page", [8, 12, 32])
 def test_store_kvcache_other_page_sizes_bit_exact(page, cuda_device):
     """The write accepts any page size: powers of two split the slot by a shift, others by a division."""
