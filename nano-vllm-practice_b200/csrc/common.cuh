@@ -180,69 +180,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ---------------------------------------------------------------------------
-// Clusters of CTAs: rank, peer shared-memory addresses, remote mbarrier arrival,
-// cluster-wide barrier.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// shared::cluster address of the object at `p` (a shared::cta pointer) in CTA `rank`.
-__device__ __forceinline__ uint32_t cluster_smem_addr(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
-
-// One arrival on an mbarrier given by its shared::cluster address (possibly in another CTA of
-// the cluster), with the instruction's default semantics, as CUTLASS's ClusterBarrier does;
-// the data it hands over is ordered by the tcgen05 / proxy fences the callers issue.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-// Make initialized mbarriers visible to the other CTAs of the cluster.
-__device__ __forceinline__ void fence_mbar_init_cluster() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-// Every thread of every CTA of the cluster (all threads of a warp together).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// mbar_wait for a barrier that other CTAs of the cluster arrive on (acquire at
-// cluster scope), with the same bound and error report.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int site) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const unsigned long long t0 = global_timer_ns();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 64; ++i) {
-      if (mbar_try_wait_cluster(bar, parity)) return true;
-    }
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
-      record_error(err, FVB_ERR_DEVICE_TIMEOUT, site);
-      return false;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Bulk copies (TMA engine), global -> shared, completion on an mbarrier.
 // No multicast form is used anywhere in this library.
 // ---------------------------------------------------------------------------

@@ -157,43 +157,4 @@ __device__ __forceinline__ void tmem_st_64cols(uint32_t taddr, const uint32_t (&
       : "memory");
 }
 
-// ---------------------------------------------------------------------------
-// CTA pairs (cta_group::2): one MMA spans the tensor cores of two SMs of a
-// cluster of two.  A is split by rows (each CTA its M/2 rows from its own
-// shared memory), B by columns (each CTA N/2 rows of B^T), D by rows (each
-// CTA's TMEM holds its M/2 rows x N columns).  Allocation, MMA and commit
-// below are the cta_group::2 forms of the instructions above.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// Issued by one thread of the pair's first CTA; descriptors name the same
-// shared-memory offsets in both CTAs.
-__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on the mbarrier at offset `bar` in every CTA of `cta_mask` when all
-// tcgen05 operations this thread issued so far have completed.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
-}
-
 }  // namespace fvb
