@@ -149,15 +149,20 @@ def test_store_kvcache_sweep_bit_exact(dtype, cuda_device):
     assert torch.equal(kp.cpu(), kref) and torch.equal(vp.cpu(), vref)
 
 
-@pytest.mark.parametrize("layout", ["head_major_view", "unaligned"])
-def test_store_kvcache_layouts_bit_exact(layout, cuda_device):
-    """Rows whose heads are not adjacent (one bulk copy per row) and rows that are not 16-byte aligned
-    (the vector kernel) write the same pools as the reference loop."""
-    T, hkv, d = 77, 4, 128
+@pytest.mark.parametrize("T", [77, 5000])
+@pytest.mark.parametrize("layout", ["contiguous", "head_major_view", "unaligned"])
+def test_store_kvcache_layouts_bit_exact(layout, T, cuda_device):
+    """The write path for each input layout and size: 5000 tokens of 16-byte-aligned rows take the bulk
+    copies (one per token and tensor when a token's heads are adjacent, one per row otherwise); 77 tokens
+    and rows off a 16-byte boundary take the vector kernel.  Every case writes the pools the reference
+    loop writes, bit for bit."""
+    hkv, d = 4, 128
     g = torch.Generator().manual_seed(31)
     kh = torch.randn(hkv, T, d, generator=g).to(torch.bfloat16)
     vh = torch.randn(hkv, T, d, generator=g).to(torch.bfloat16)
-    if layout == "head_major_view":  # (T, Hkv, D) view of head-major storage: head stride T * D
+    if layout == "contiguous":
+        k, v = kh.transpose(0, 1).contiguous().to(cuda_device), vh.transpose(0, 1).contiguous().to(cuda_device)
+    elif layout == "head_major_view":  # (T, Hkv, D) view of head-major storage: head stride T * D
         k, v = kh.to(cuda_device).transpose(0, 1), vh.to(cuda_device).transpose(0, 1)
     else:  # one element past a 16-byte boundary
         flat = torch.empty(2 * T * hkv * d + 2, dtype=torch.bfloat16, device=cuda_device)
@@ -168,16 +173,20 @@ def test_store_kvcache_layouts_bit_exact(layout, cuda_device):
     nb = (2 * T + 15) // 16
     slots = torch.randperm(nb * 16, generator=g)[:T].to(torch.int64)
     slots[3] = -1
+    slots[T - 1] = -1  # a padding token in the last chunk too
+    bad = T - 7
+    slots[bad] = nb * 16  # one past the pool: reported, skipped, the rest still written
     kref = torch.zeros(nb, hkv, 16, d, dtype=torch.bfloat16)
     vref = torch.zeros_like(kref)
     kp, vp = kref.to(cuda_device), vref.to(cuda_device)
+    cabi.read_device_error()
     cabi.store_kvcache(k, v, kp, vp, slots.to(cuda_device))
     s = slots.numpy()
-    live = s >= 0
+    live = (s >= 0) & (s < nb * 16)
     kref[s[live] // 16, :, s[live] % 16] = kh.transpose(0, 1)[live]
     vref[s[live] // 16, :, s[live] % 16] = vh.transpose(0, 1)[live]
     assert torch.equal(kp.cpu(), kref) and torch.equal(vp.cpu(), vref)
-    assert cabi.read_device_error() == (0, 0)
+    assert cabi.read_device_error() == (8, bad)  # FVB_ERR_BAD_SLOT at that token
 
 
 @pytest.mark.parametrize("page", [8, 12, 32])
