@@ -31,6 +31,8 @@
 // (Hq + 2 Hkv) D sizeof(T) bytes read and written per token, plus 12 bytes
 // of position / slot and the cos / sin rows (L2-resident).  The arithmetic is
 // in packed fp32x2 (FFMA2 / FMUL2) to keep the issue rate below the memory rate.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -91,10 +93,12 @@ constexpr int kThreads = 256;
 // so the norm weights are loaded once, position / slot / cos / sin once per
 // token, and only the rows themselves per head.  Three CTAs per SM (80
 // registers, no spills) measured faster than four (64 registers, spills).
-template <typename T, int D>
+// I is the type of every element offset: int when all of the launch's tensors are
+// smaller than 2^31 elements (3.3 % faster at config 3's tokens), int64_t otherwise.
+template <typename T, int D, typename I>
 __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
-    const T* __restrict__ q, int64_t q_ts, int64_t q_hs, const T* __restrict__ k, int64_t k_ts, int64_t k_hs,
-    const T* __restrict__ v, int64_t v_ts, int64_t v_hs, const T* __restrict__ q_w, const T* __restrict__ k_w,
+    const T* __restrict__ q, I q_ts, I q_hs, const T* __restrict__ k, I k_ts, I k_hs,
+    const T* __restrict__ v, I v_ts, I v_hs, const T* __restrict__ q_w, const T* __restrict__ k_w,
     float eps, const T* __restrict__ cos_t, const T* __restrict__ sin_t, int rope_rows,
     const int32_t* __restrict__ positions, const int64_t* __restrict__ slot_mapping, int num_tokens,
     int n_heads, int n_kv_heads, T* __restrict__ q_out, T* __restrict__ k_pool, T* __restrict__ v_pool,
@@ -164,9 +168,9 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
   };
 
   auto load_row = [&](int t, int uu) -> uint4 {
-    if (uu < n_heads) return ldg_pair<T, D>(q + int64_t(t) * q_ts + uu * q_hs, sub);
-    if (uu < n_heads + n_kv_heads) return ldg_pair<T, D>(k + int64_t(t) * k_ts + (uu - n_heads) * k_hs, sub);
-    return ldg16(v + int64_t(t) * v_ts + (uu - n_heads - n_kv_heads) * v_hs + sub * E);
+    if (uu < n_heads) return ldg_pair<T, D>(q + (I(t) * q_ts + I(uu) * q_hs), sub);
+    if (uu < n_heads + n_kv_heads) return ldg_pair<T, D>(k + (I(t) * k_ts + I(uu - n_heads) * k_hs), sub);
+    return ldg16(v + (I(t) * v_ts + I(uu - n_heads - n_kv_heads) * v_hs + I(sub * E)));
   };
   const int tstride = gridDim.x * tpb;
   int t = blockIdx.x * tpb + tok_off;
@@ -187,26 +191,26 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
     const bool rope_ok = pos >= 0 && pos < rope_rows;
     uint4 c = make_uint4(0, 0, 0, 0), sn = make_uint4(0, 0, 0, 0);
     if (rope_ok) {
-      c = ldg_pair<T, D>(cos_t + int64_t(pos) * D, sub);
-      sn = ldg_pair<T, D>(sin_t + int64_t(pos) * D, sub);
+      c = ldg_pair<T, D>(cos_t + I(pos) * D, sub);
+      sn = ldg_pair<T, D>(sin_t + I(pos) * D, sub);
     }
     if (slot >= num_slots) {
       if (sub == 0) record_error(err, FVB_ERR_BAD_SLOT, t);
       slot = -1;
     }
     if (!rope_ok && u0 == 0 && sub == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, t);
-    const int64_t blk = slot < 0 ? 0 : block_shift >= 0 ? (slot >> block_shift) : slot / block_size;
-    const int off = slot >= 0 ? int(slot - blk * block_size) : 0;
+    const I blk = slot < 0 ? 0 : block_shift >= 0 ? I(slot >> block_shift) : I(slot / block_size);
+    const int off = slot >= 0 ? int(slot - int64_t(blk) * block_size) : 0;
     auto finish = [&](int uu, const uint4& raw) {
       if (uu < n_heads) {
-        if (rope_ok) st_pair<T, D>(q_out + (int64_t(uu) * num_tokens + t) * D, sub, norm_rope(raw, wq, c, sn));
+        if (rope_ok) st_pair<T, D>(q_out + (I(uu) * num_tokens + t) * D, sub, norm_rope(raw, wq, c, sn));
       } else if (uu < n_heads + n_kv_heads) {
         if (rope_ok && slot >= 0)
-          st_pair<T, D>(k_pool + ((blk * n_kv_heads + (uu - n_heads)) * block_size + off) * D, sub,
+          st_pair<T, D>(k_pool + ((blk * n_kv_heads + (uu - n_heads)) * block_size + off) * I(D), sub,
                         norm_rope(raw, wk, c, sn));
       } else if (slot >= 0) {  // value row: bit-exact copy
-        *reinterpret_cast<uint4*>(v_pool + ((blk * n_kv_heads + (uu - n_heads - n_kv_heads)) * block_size + off) * D +
-                                  sub * E) = raw;
+        *reinterpret_cast<uint4*>(v_pool + (((blk * n_kv_heads + (uu - n_heads - n_kv_heads)) * block_size + off) * I(D) +
+                                            I(sub * E))) = raw;
       }
     };
     finish(u0, ra);
@@ -239,12 +243,24 @@ cudaError_t launch_typed(const void* q, int64_t q_ts, int64_t q_hs, const void* 
   int block_shift = -1;  // page size a power of two: slot / block_size as a shift
   for (int b = 0; b < 31; ++b)
     if ((1 << b) == block_size) block_shift = b;
-  qk_norm_rope_store_kernel<T, D><<<unsigned(blocks), kThreads, 0, stream>>>(
-      static_cast<const T*>(q), q_ts, q_hs, static_cast<const T*>(k), k_ts, k_hs, static_cast<const T*>(v), v_ts,
-      v_hs, static_cast<const T*>(q_w), static_cast<const T*>(k_w), eps, static_cast<const T*>(cos_t),
-      static_cast<const T*>(sin_t), rope_rows, positions, slot_mapping, int(num_tokens), n_heads, n_kv_heads,
-      static_cast<T*>(q_out), static_cast<T*>(k_pool), static_cast<T*>(v_pool), num_blocks * block_size, block_size,
-      block_shift, err);
+  // Largest element offset any thread forms, in each tensor.
+  auto span = [&](int64_t ts, int64_t hs, int heads) { return (num_tokens - 1) * ts + int64_t(heads - 1) * hs + D; };
+  const int64_t widest = std::max({span(q_ts, q_hs, n_heads), span(k_ts, k_hs, n_kv_heads), span(v_ts, v_hs, n_kv_heads),
+                                   int64_t(n_heads) * num_tokens * D, num_blocks * n_kv_heads * block_size * D,
+                                   int64_t(rope_rows) * D});
+#define FVB_QKN_LAUNCH(I)                                                                                              \
+  qk_norm_rope_store_kernel<T, D, I><<<unsigned(blocks), kThreads, 0, stream>>>(                                      \
+      static_cast<const T*>(q), I(q_ts), I(q_hs), static_cast<const T*>(k), I(k_ts), I(k_hs),                         \
+      static_cast<const T*>(v), I(v_ts), I(v_hs), static_cast<const T*>(q_w), static_cast<const T*>(k_w), eps,       \
+      static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), rope_rows, positions, slot_mapping,                \
+      int(num_tokens), n_heads, n_kv_heads, static_cast<T*>(q_out), static_cast<T*>(k_pool), static_cast<T*>(v_pool), \
+      num_blocks * block_size, block_size, block_shift, err)
+  if (widest < (int64_t(1) << 31)) {
+    FVB_QKN_LAUNCH(int);
+  } else {
+    FVB_QKN_LAUNCH(int64_t);
+  }
+#undef FVB_QKN_LAUNCH
   return cudaGetLastError();
 }
 
