@@ -279,3 +279,40 @@ def test_other_page_sizes_write_the_same_rows(page, cuda_device):
         assert torch.equal(a, b)
     assert torch.equal(run(page)[2], v.cpu())
 
+
+
+def test_pools_past_2_31_elements_write_the_same_rows(cuda_device):
+    """Pools of more than 2^31 elements take the 64-bit-offset kernel: its q_out and the rows it writes near
+    the top of such a pool equal what the 32-bit-offset kernel writes into a small pool."""
+    T, hq, hkv, d = 96, 8, 8, 128
+    g = torch.Generator().manual_seed(77)
+    x = torch.randn(T, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16).to(cuda_device)
+    q = x[:, : hq * d].view(T, hq, d)
+    k = x[:, hq * d : (hq + hkv) * d].view(T, hkv, d)
+    v = x[:, (hq + hkv) * d :].view(T, hkv, d)
+    q_w, k_w = _weights(d, torch.bfloat16, cuda_device, seed=77)
+    cos, sin = _rope(256, d, torch.bfloat16, cuda_device)
+    positions = torch.randint(0, 256, (T,), generator=g, dtype=torch.int32).to(cuda_device)
+    small_blocks = 16
+    rel = torch.randperm(small_blocks * 16, generator=g)[:T].to(torch.int64)
+    big_blocks = (1 << 31) // (hkv * 16 * d) + 64  # 2^31 elements per pool and a little more: 4.3 GB each
+    base = (big_blocks - small_blocks) * 16  # the same rows, at the top of the big pool
+
+    def run(nb, offset):
+        kp = torch.zeros(nb, hkv, 16, d, dtype=torch.bfloat16, device=cuda_device)
+        vp = torch.zeros_like(kp)
+        slots = (rel + offset).to(cuda_device)
+        cabi.read_device_error()
+        q_out = cabi.qk_norm_rope_store(q, k, v, q_w, k_w, 1e-6, cos, sin, positions, kp, vp, slots)
+        assert cabi.read_device_error() == (0, 0)
+        sl = slots.cpu()
+        rows = (kp[sl // 16, :, sl % 16].cpu(), vp[sl // 16, :, sl % 16].cpu())
+        del kp, vp
+        torch.cuda.empty_cache()
+        return (q_out.cpu(),) + rows
+
+    small = run(small_blocks, 0)
+    big = run(big_blocks, base)
+    for a, b in zip(small, big):
+        assert torch.equal(a, b)
+    assert torch.equal(big[2], v.cpu())
