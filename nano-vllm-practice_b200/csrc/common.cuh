@@ -222,6 +222,45 @@ __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents lets a kernel launched after
+// this one with cudaLaunchAttributeProgrammaticStreamSerialization start once every
+// CTA of this grid has executed it (or exited); that kernel's grid_dependency_wait
+// returns when this grid has completed and its memory writes are visible.  Both are
+// no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Named barrier over nthreads threads that also returns the AND of pred over them.
+__device__ __forceinline__ bool named_barrier_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(pred)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+// Asynchronous global -> shared copies of 16, 8 or 4 bytes (cp.async), tracked per
+// thread in commit groups: no register holds the data while it is in flight.
+// Addresses must be aligned to the copy size.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's most recent commit groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Read-only 16-byte global load that does not allocate in L1.
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 r;

@@ -31,7 +31,7 @@
 // At the end the four warps' (max, sum, acc) are merged in shared memory; a
 // sequence with a single split writes its output directly, otherwise the
 // normalised partial and its log-sum-exp go to the workspace and
-// decode_combine_kernel merges the splits.
+// decode_combine_kernel, launched as a programmatic dependent, merges the splits.
 #include <algorithm>
 
 #include "common.cuh"
@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     int kv_cap, int pages_per_split, int max_splits, float* __restrict__ ws_o, float* __restrict__ ws_lse,
     const QOLayout lay, int group, int chunks, int* __restrict__ err) {
   using Tr = DecodeTraits<T, D, NREP>;
+  launch_dependents();  // the combine may take free SM slots once every split CTA is resident
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   T* qs = reinterpret_cast<T*>(smem + Tr::kOffQ);
@@ -382,60 +383,127 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
 }
 
 // Merge the split partials of every (sequence, head) that has more than one
-// split.  One CTA per (sequence, head), one thread per head dim: the split
-// weights 2^(lse_s - max) are computed once into shared memory, then every
-// thread sums its column of the partial rows (coalesced across threads).
+// split.  One CTA of kCmbThreads per (sequence, head).  A partial row (D fp32) is
+// read by D / 4 threads with 16-byte loads, so the CTA covers kGroups rows per pass;
+// thread (g, c) walks rows g, g + kGroups, ... with kCmbUnroll rows in flight and
+// keeps an online log2-sum-exp merge of them (running max m, sum l and the
+// weighted column sums), and the kGroups row groups are merged in shared memory.
+// The many independent 16-byte loads per CTA keep the partials streaming; one
+// load per thread and split (a CTA per head with a thread per dim) left the merge
+// latency-bound at long contexts, where a sequence has ~100 splits.
+//
+// Launched as a programmatic dependent of the split kernel (which triggers at its
+// start): its CTAs take free SM slots during the split kernel's last wave and
+// wait in grid_dependency_wait until the partials are complete.
+constexpr int kCmbThreads = 256;
+constexpr int kCmbUnroll = 4;
+
+template <typename T>
+__device__ __forceinline__ void store4(T* p, const float4& v) {
+  if constexpr (sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(p) = v;
+  } else {
+    __align__(8) T h[4] = {Elem<T>::from_f(v.x), Elem<T>::from_f(v.y), Elem<T>::from_f(v.z), Elem<T>::from_f(v.w)};
+    *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(h);
+  }
+}
+
 template <typename T, int D>
-__global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restrict__ ws_o,
-                                                           const float* __restrict__ ws_lse, T* __restrict__ out,
-                                                           const int32_t* __restrict__ kv_lens, int kv_cap,
-                                                           int num_seqs, int n_heads, int pages_per_split,
-                                                           int max_splits, const QOLayout lay) {
-  extern __shared__ float wsh[];  // [max_splits] weights, then [D / 32] partial maxima / sums
-  float* red = wsh + max_splits;
+__global__ void __launch_bounds__(kCmbThreads) decode_combine_kernel(const float* __restrict__ ws_o,
+                                                                     const float* __restrict__ ws_lse,
+                                                                     T* __restrict__ out,
+                                                                     const int32_t* __restrict__ kv_lens, int kv_cap,
+                                                                     int num_seqs, int n_heads, int pages_per_split,
+                                                                     int max_splits, const QOLayout lay) {
+  constexpr int kLanes = D / 4;                  // threads per partial row
+  constexpr int kGroups = kCmbThreads / kLanes;  // rows per pass: 8 (D 128) or 16 (D 64)
+  __shared__ float4 g_acc[kGroups][kLanes];
+  __shared__ float g_m[kGroups], g_l[kGroups];
   const int b = blockIdx.x / n_heads, head = blockIdx.x % n_heads;
-  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  // kv_lens was written before the split kernel started, so it is read before the wait.
   const int kv_len = min(max(__ldg(kv_lens + b), 0), kv_cap);
   const int npages = (kv_len + kPageSize - 1) / kPageSize;
   const int nsplits = (npages + pages_per_split - 1) / pages_per_split;
   if (nsplits <= 1) return;  // written directly by the split kernel
+  grid_dependency_wait();
+  const int g = threadIdx.x / kLanes, c = threadIdx.x % kLanes;
   const int64_t base = (int64_t(b) * n_heads + head) * max_splits;
-  float mx = -INFINITY;
-  for (int s = d; s < nsplits; s += D) {
-    const float v = __ldg(ws_lse + base + s);
-    wsh[s] = v;
-    mx = fmaxf(mx, v);
-  }
-  mx = warp_max(mx);
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  mx = red[0];
+  const float4* src = reinterpret_cast<const float4*>(ws_o + base * D) + c;
+  float m = -INFINITY, l = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = g; s0 < nsplits; s0 += kCmbUnroll * kGroups) {
+    float4 o[kCmbUnroll];
+    float ls[kCmbUnroll];
 #pragma unroll
-  for (int w = 1; w < D / 32; ++w) mx = fmaxf(mx, red[w]);
+    for (int u = 0; u < kCmbUnroll; ++u) {
+      const int s = s0 + u * kGroups;
+      const bool in = s < nsplits;
+      // L2-coherent loads (.cg): the rows were written by the previous grid.
+      o[u] = in ? __ldcg(src + int64_t(s) * kLanes) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ls[u] = in ? __ldcg(ws_lse + base + s) : -INFINITY;
+    }
+    float mn = m;
+#pragma unroll
+    for (int u = 0; u < kCmbUnroll; ++u) mn = fmaxf(mn, ls[u]);  // finite: row s0 exists
+    const float corr = fast_exp2(m - mn);                        // 0 on the first pass
+    l *= corr;
+    acc.x *= corr;
+    acc.y *= corr;
+    acc.z *= corr;
+    acc.w *= corr;
+#pragma unroll
+    for (int u = 0; u < kCmbUnroll; ++u) {
+      const float w = fast_exp2(ls[u] - mn);  // 0 for rows past nsplits
+      l += w;
+      acc.x = fmaf(w, o[u].x, acc.x);
+      acc.y = fmaf(w, o[u].y, acc.y);
+      acc.z = fmaf(w, o[u].z, acc.z);
+      acc.w = fmaf(w, o[u].w, acc.w);
+    }
+    m = mn;
+  }
+  g_acc[g][c] = acc;  // groups without rows leave m = -inf, l = 0, acc = 0
+  if (c == 0) {
+    g_m[g] = m;
+    g_l[g] = l;
+  }
   __syncthreads();
+  if (g != 0) return;
+  float M = g_m[0];  // finite: group 0 holds split 0
+#pragma unroll
+  for (int k = 1; k < kGroups; ++k) M = fmaxf(M, g_m[k]);
   float L = 0.f;
-  for (int s = d; s < nsplits; s += D) {
-    const float w = fast_exp2(wsh[s] - mx);
-    wsh[s] = w;
-    L += w;
-  }
-  L = warp_sum(L);
-  if (lane == 0) red[warp] = L;
-  __syncthreads();
-  L = red[0];
+  float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int w = 1; w < D / 32; ++w) L += red[w];
-  const float* src = ws_o + base * D + d;
-  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-  int s = 0;
-  for (; s + 4 <= nsplits; s += 4) {
-    o0 = fmaf(wsh[s], __ldg(src + int64_t(s) * D), o0);
-    o1 = fmaf(wsh[s + 1], __ldg(src + int64_t(s + 1) * D), o1);
-    o2 = fmaf(wsh[s + 2], __ldg(src + int64_t(s + 2) * D), o2);
-    o3 = fmaf(wsh[s + 3], __ldg(src + int64_t(s + 3) * D), o3);
+  for (int k = 0; k < kGroups; ++k) {
+    const float w = fast_exp2(g_m[k] - M);
+    const float4 a = g_acc[k][c];
+    L = fmaf(g_l[k], w, L);
+    O.x = fmaf(a.x, w, O.x);
+    O.y = fmaf(a.y, w, O.y);
+    O.z = fmaf(a.z, w, O.z);
+    O.w = fmaf(a.w, w, O.w);
   }
-  for (; s < nsplits; ++s) o0 = fmaf(wsh[s], __ldg(src + int64_t(s) * D), o0);
-  out[int64_t(b) * lay.o_ts + int64_t(head) * lay.o_hs + d] = Elem<T>::from_f(((o0 + o1) + (o2 + o3)) / L);
+  store4(out + int64_t(b) * lay.o_ts + int64_t(head) * lay.o_hs + 4 * c,
+         make_float4(O.x / L, O.y / L, O.z / L, O.w / L));
+}
+
+template <typename T, int D>
+cudaError_t launch_combine_t(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens, int kv_cap,
+                             int num_seqs, int n_heads, int pages_per_split, int max_splits, const QOLayout& lay,
+                             cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(num_seqs) * unsigned(n_heads));
+  cfg.blockDim = dim3(kCmbThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, D>, ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap,
+                            num_seqs, n_heads, pages_per_split, max_splits, lay);
 }
 
 template <typename T, int D, int NREP>
@@ -471,15 +539,8 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
       ws_o, ws_lse, lay, group, chunks, err);
   ce = cudaGetLastError();
   if (ce != cudaSuccess || plan.max_splits <= 1) return ce;
-  const size_t csmem = (size_t(plan.max_splits) + D / 32) * sizeof(float);
-  if (csmem > 48 * 1024) {
-    ce = cudaFuncSetAttribute(decode_combine_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(csmem));
-    if (ce != cudaSuccess) return ce;
-  }
-  decode_combine_kernel<T, D><<<unsigned(num_seqs * n_kv_heads * group), D, csmem, stream>>>(
-      ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap, num_seqs, n_kv_heads * group, plan.pages_per_split,
-      plan.max_splits, lay);
-  return cudaGetLastError();
+  return launch_combine_t<T, D>(ws_o, ws_lse, out, kv_lens, kv_cap, num_seqs, n_kv_heads * group,
+                                plan.pages_per_split, plan.max_splits, lay, stream);
 }
 
 template <typename T, int D>
@@ -548,22 +609,6 @@ cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const vo
 #undef FVB_DECODE_ARGS
 }
 
-namespace {
-template <typename T, int D>
-cudaError_t launch_combine_t(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens, int kv_cap,
-                             int num_seqs, int n_heads, int pages_per_split, int max_splits, const QOLayout& lay,
-                             cudaStream_t stream) {
-  const size_t csmem = (size_t(max_splits) + D / 32) * sizeof(float);
-  if (csmem > 48 * 1024) {
-    cudaError_t ce =
-        cudaFuncSetAttribute(decode_combine_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(csmem));
-    if (ce != cudaSuccess) return ce;
-  }
-  decode_combine_kernel<T, D><<<unsigned(num_seqs * n_heads), D, csmem, stream>>>(
-      ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap, num_seqs, n_heads, pages_per_split, max_splits, lay);
-  return cudaGetLastError();
-}
-}  // namespace
 
 cudaError_t launch_decode_combine(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens,
                                   int kv_cap, int num_seqs, int n_heads, int head_dim, int pages_per_split,
