@@ -242,25 +242,6 @@ __device__ __forceinline__ bool named_barrier_and(int id, int nthreads, bool pre
   return r != 0;
 }
 
-// Asynchronous global -> shared copies of 16, 8 or 4 bytes (cp.async), tracked per
-// thread in commit groups: no register holds the data while it is in flight.
-// Addresses must be aligned to the copy size.
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// Wait until at most N of this thread's most recent commit groups are pending.
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Read-only 16-byte global load that does not allocate in L1.
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 r;
