@@ -551,7 +551,7 @@ def _prefill_like_block(ctx, batch, key, with_reference_triton):
     pipe = HostPipeline(ctx.dev, (batch.q, cu, tab, lens, pos), batch.q.shape, batch.q.dtype)
     e2e_first, e2e_med = pipe.timed(ctx, lambda v: call(v[0], v[1], v[2], v[3], v[4]))
     res = {"ms": first, "ms_median": med, "blocks": blocks, "clocks": clocks, "flops": batch.attn_flops(),
-           "kv_bytes": batch.kv_bytes(), "tokens": batch.num_tokens, "e2e_ms": e2e_first, "e2e_ms_median": e2e_med,
+           "kv_bytes": batch.kv_bytes(), "kv_bytes_unique": batch.unique_kv_bytes(), "tokens": batch.num_tokens, "e2e_ms": e2e_first, "e2e_ms_median": e2e_med,
            "h2d": pipe.h2d_bytes, "d2h": pipe.d2h_bytes, "name": batch.name}
     del pipe
     if with_reference_triton:
@@ -711,6 +711,7 @@ def line_prefill(ctx, g, workload, config):
                       "blocks": min(x["blocks"] for x in g)},
         "tokens_per_s": _r(tokens / (t * 1e-3), 1),
         "gbs_kv": _r(sum(x["kv_bytes"] for x in g) / (t * 1e-3) / 1e9, 1),
+        "gbs_kv_unique": _r(sum(x["kv_bytes_unique"] for x in g) / (t * 1e-3) / 1e9, 1),
         "flops_per_step_per_gpu": r0["flops"],
         "roofline": {
             "kernel": "prefill_plan_kernel + prefill_tc_kernel (one paged_attention_gemm call)",

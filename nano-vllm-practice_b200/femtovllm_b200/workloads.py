@@ -92,6 +92,14 @@ class PagedBatch:
         es = torch.finfo(self.dtype).bits // 8
         return int(2 * self.kv_lens.astype(np.int64).sum() * self.n_kv_heads * self.head_dim * es)
 
+    def unique_kv_bytes(self) -> int:
+        """K+V bytes of the distinct pages the launch attends over (a page shared by several
+        requests' tables, as config 4's common prefix, counted once)."""
+        es = torch.finfo(self.dtype).bits // 8
+        npages = (self.kv_lens.astype(np.int64) + PAGE - 1) // PAGE
+        pages = np.concatenate([self.block_tables[s, : int(n)] for s, n in enumerate(npages)])
+        return int(2 * np.unique(pages).size * PAGE * self.n_kv_heads * self.head_dim * es)
+
     def decode_bytes(self) -> int:
         """Algorithmic HBM bytes of one decode launch: K+V, q, out, block tables, kv_lens."""
         es = torch.finfo(self.dtype).bits // 8
