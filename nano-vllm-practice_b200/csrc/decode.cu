@@ -571,11 +571,15 @@ DecodePlan plan_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, 
   const int group = n_kv_heads > 0 ? n_heads / n_kv_heads : 1;
   const int tile = decode_tile_heads(group);
   const int64_t units = int64_t(num_seqs) * n_kv_heads * ((group + tile - 1) / tile);
-  // Enough CTAs for ~4 waves of 3 resident CTAs per SM, but no split shorter
-  // than 4 pages (64 tokens) and none longer than 64 pages (1024 tokens), so
-  // the last wave's tail stays short for long contexts.
+  // Splits of up to 256 pages (4096 tokens): each CTA start costs a pipeline fill
+  // and drain, which at 1024-token splits held config 5 (32k-131k tokens) 5-8 %
+  // below the longer splits.  The longest sequence keeps at least 4 splits down to
+  // 64 pages (config 2's 512-4096 tokens keep 1024-token splits, whose shorter
+  // tail measured 0.6 % faster there), and splits halve (down to 4 pages) until
+  // there are enough CTAs for ~4 waves of 3 resident CTAs per SM.
   const int64_t target = int64_t(num_sms) * 3 * 4;
-  int pps = 64;
+  int pps = 256;
+  while (pps > 64 && max_pages < 4 * pps) pps /= 2;
   while (pps > 4 && units * ((max_pages + pps - 1) / pps) < target) pps /= 2;
   p.pages_per_split = pps;
   p.max_splits = (max_pages + pps - 1) / pps;
