@@ -118,8 +118,11 @@ def test_decode_workspace_plan(lib):
     # Plenty of (seq, kv head) units and short contexts: no split, no workspace.
     assert lib.fvb_paged_attention_decode_workspace_size(1024, 16, 8, 128, 512) == 0
     # Long contexts split; the workspace holds a partial row + a log-sum-exp per (seq, head, split).
+    # (131,072 tokens over 8 sequences: 4096-token splits, 32 per sequence)
     ws = lib.fvb_paged_attention_decode_workspace_size(8, 32, 8, 128, 131072)
-    assert ws >= 8 * 32 * (131072 // 1024) * 129 * 4
+    assert ws >= 8 * 32 * (131072 // 4096) * 129 * 4
+    # config-2 lengths keep 1024-token splits
+    assert lib.fvb_paged_attention_decode_workspace_size(16, 16, 8, 128, 4096) >= 16 * 16 * 4 * 129 * 4
     assert lib.fvb_paged_attention_decode_workspace_size(0, 32, 8, 128, 131072) == 0
 
 
