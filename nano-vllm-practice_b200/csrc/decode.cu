@@ -572,9 +572,9 @@ DecodePlan plan_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, 
   const int tile = decode_tile_heads(group);
   const int64_t units = int64_t(num_seqs) * n_kv_heads * ((group + tile - 1) / tile);
   // Splits of up to 256 pages (4096 tokens): each CTA start costs a pipeline fill
-  // and drain, which at 1024-token splits held config 5 (32k-131k tokens) 5-8 %
+  // and drain, which at 1024-token splits held 32k-131k-token contexts 5-8 %
   // below the longer splits.  The longest sequence keeps at least 4 splits down to
-  // 64 pages (config 2's 512-4096 tokens keep 1024-token splits, whose shorter
+  // 64 pages (contexts of 512-4096 tokens keep 1024-token splits, whose shorter
   // tail measured 0.6 % faster there), and splits halve (down to 4 pages) until
   // there are enough CTAs for ~4 waves of 3 resident CTAs per SM.
   const int64_t target = int64_t(num_sms) * 3 * 4;

@@ -94,7 +94,7 @@ class PagedBatch:
 
     def unique_kv_bytes(self) -> int:
         """K+V bytes of the distinct pages the launch attends over (a page shared by several
-        requests' tables, as config 4's common prefix, counted once)."""
+        requests' tables, as a common prefix, counted once)."""
         es = torch.finfo(self.dtype).bits // 8
         npages = (self.kv_lens.astype(np.int64) + PAGE - 1) // PAGE
         pages = np.concatenate([self.block_tables[s, : int(n)] for s, n in enumerate(npages)])
