@@ -83,20 +83,43 @@ __device__ __forceinline__ void st_pair(T* row, int sub, const uint4& v) {
   *reinterpret_cast<uint2*>(row + D / 2 + sub * H) = make_uint2(v.z, v.w);
 }
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 192;         // q / k rows
+constexpr int kVThreads = 32;         // one warp copying the value rows with bulk copies
+constexpr int kAllThreads = kThreads + kVThreads;
+constexpr int kCtasPerSm = 4;
+constexpr int kVStages = 4;           // value-row stages of the copy warp
+constexpr int kVStageMax = 8 * 1024;  // value bytes of one block pass (else the q / k threads copy them)
 
-// Work split.  A row is one head of one token; a block has S = kThreads / L
-// row slots.  With units = Hq + 2 Hkv heads per token, a block takes
+__device__ __forceinline__ void bulk_s2g_v(void* dst_gmem, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem), "r"(src_smem),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_v() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_reads_v() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_done_v() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Work split.  A block is kThreads q / k threads plus one copy warp.  A row is
+// one head of one token; the q / k threads form S = kThreads / L row slots.
+// The copy warp moves the value rows (a bit-exact copy) with bulk copies:
+// global -> shared (one copy per token when its heads are contiguous) ->
+// each row's pool slot, kVStages block passes deep, so those bytes are in
+// flight without registers while the q / k threads take only the q and k
+// rows: units = Hq + Hkv heads per token (Hq + 2 Hkv when a pass's value rows
+// exceed kVStageMax and the q / k threads copy them too).  A block takes
 // S / units whole tokens per pass when units <= S (slot j -> token j / units,
 // head j % units), otherwise one token per pass with slot j taking heads
 // j, j + S, j + 2S, ...  Each thread's heads are fixed for the whole launch,
 // so the norm weights are loaded once, position / slot / cos / sin once per
-// token, and only the rows themselves per head.  Three CTAs per SM (80
-// registers, no spills) measured faster than four (64 registers, spills).
+// token, and only the rows themselves per head.  Measured on 65k tokens of
+// Hq 16 / Hkv 8 (bf16, D 128): 4.54 TB/s with 256 threads copying every row
+// (3 CTAs per SM, 80 registers), 5.01 TB/s with 192 q / k threads + the copy
+// warp at 4 CTAs per SM; 3 or 5 CTAs per SM, 128 or 256 q / k threads and 8
+// value stages were slower.
 // I is the type of every element offset: int when all of the launch's tensors are
 // smaller than 2^31 elements (3.3 % faster on 65k tokens of 32 heads), int64_t otherwise.
-template <typename T, int D, typename I>
-__global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
+template <typename T, int D, typename I, bool VT>
+__global__ void __launch_bounds__(kAllThreads, kCtasPerSm) qk_norm_rope_store_kernel(
     const T* __restrict__ q, I q_ts, I q_hs, const T* __restrict__ k, I k_ts, I k_hs,
     const T* __restrict__ v, I v_ts, I v_hs, const T* __restrict__ q_w, const T* __restrict__ k_w,
     float eps, const T* __restrict__ cos_t, const T* __restrict__ sin_t, int rope_rows,
@@ -109,12 +132,77 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
   constexpr int S = kThreads / L;         // row slots per block
   static_assert(L >= 2 && L <= 32 && 32 % L == 0, "row must tile a warp");
   static_assert(E % 2 == 0, "pairs of elements");
-  const int units = n_heads + 2 * n_kv_heads;
+  // VT: value rows go through the copy warp (bulk copies, global -> shared -> pool rows); the
+  // q / k threads then take only the Hq + Hkv q and k rows of a token.
+  const int units = n_heads + (VT ? 1 : 2) * n_kv_heads;
   const int lane = threadIdx.x & 31;
-  const int sub = threadIdx.x % L;
-  const int j = threadIdx.x / L;
   const bool packed = units <= S;
   const int tpb = packed ? S / units : 1;  // tokens per block pass
+  const int tstride = gridDim.x * tpb;
+  if (threadIdx.x >= kThreads) {
+    // ======================== value rows: global -> shared -> pool, bulk copies ========================
+    if constexpr (VT) {
+      extern __shared__ __align__(128) uint8_t vsm[];
+      constexpr int ROW = D * int(sizeof(T));
+      const int pass_bytes = tpb * n_kv_heads * ROW;
+      uint64_t* vbar = reinterpret_cast<uint64_t*>(vsm + kVStages * pass_bytes);
+      if (lane == 0) {
+        for (int i = 0; i < kVStages; ++i) mbar_init(&vbar[i], 1);
+        fence_mbar_init();
+      }
+      __syncwarp();
+      const bool heads_contiguous = v_hs == I(D);
+      auto load_pass = [&](int p) {  // lane 0
+        const int tb = blockIdx.x * tpb + p * tstride;
+        const int nt = min(tpb, num_tokens - tb);
+        const int st = p % kVStages;
+        mbar_arrive_expect_tx(&vbar[st], uint32_t(nt * n_kv_heads * ROW));
+        uint8_t* dst = vsm + st * pass_bytes;
+        for (int i = 0; i < nt; ++i) {
+          const T* src = v + I(tb + i) * v_ts;
+          if (heads_contiguous) {
+            bulk_g2s(dst + i * n_kv_heads * ROW, src, uint32_t(n_kv_heads * ROW), &vbar[st]);
+          } else {
+            for (int h = 0; h < n_kv_heads; ++h)
+              bulk_g2s(dst + (i * n_kv_heads + h) * ROW, src + I(h) * v_hs, uint32_t(ROW), &vbar[st]);
+          }
+        }
+      };
+      const int npass = blockIdx.x * tpb < num_tokens ? (num_tokens - blockIdx.x * tpb + tstride - 1) / tstride : 0;
+      if (lane == 0) {
+        for (int p = 0; p < kVStages - 1 && p < npass; ++p) load_pass(p);
+      }
+      for (int p = 0; p < npass; ++p) {
+        // the stage the next load reuses held pass p - 1: every lane's stores of it have read it
+        bulk_wait_reads_v();
+        __syncwarp();
+        if (lane == 0 && p + kVStages - 1 < npass) load_pass(p + kVStages - 1);
+        const int st = p % kVStages;
+        if (!__all_sync(0xffffffffu, mbar_wait(&vbar[st], uint32_t(p / kVStages) & 1u, err, 0x340))) {
+          // give the loads still in flight (passes p + 1 .. p + kVStages - 1) a bounded wait before exiting
+          for (int q2 = p + 1; q2 < npass && q2 < p + kVStages; ++q2)
+            mbar_wait(&vbar[q2 % kVStages], uint32_t(q2 / kVStages) & 1u, err, 0x341);
+          break;
+        }
+        const int tb = blockIdx.x * tpb + p * tstride;
+        const int nt = min(tpb, num_tokens - tb);
+        for (int rr = lane; rr < nt * n_kv_heads; rr += 32) {
+          const int i = rr / n_kv_heads, h = rr - i * n_kv_heads;
+          const int64_t slot = __ldg(slot_mapping + tb + i);
+          if (slot < 0 || slot >= num_slots) continue;  // padding, or reported by the q / k threads
+          const int64_t blk = block_shift >= 0 ? (slot >> block_shift) : slot / block_size;
+          const int off = int(slot - blk * block_size);
+          bulk_s2g_v(v_pool + ((I(blk) * n_kv_heads + h) * block_size + off) * I(D),
+                     smem_u32(vsm + st * pass_bytes + rr * ROW), uint32_t(ROW));
+        }
+        bulk_commit_v();
+      }
+      bulk_wait_done_v();  // no copy of this warp is in flight when it exits
+    }
+    return;
+  }
+  const int sub = threadIdx.x % L;
+  const int j = threadIdx.x / L;
   if (packed && j >= tpb * units) return;  // spare slot (its whole row group leaves together)
   const int tok_off = packed ? j / units : 0;
   const int u0 = packed ? j % units : j;
@@ -172,7 +260,6 @@ __global__ void __launch_bounds__(kThreads, 3) qk_norm_rope_store_kernel(
     if (uu < n_heads + n_kv_heads) return ldg_pair<T, D>(k + (I(t) * k_ts + I(uu - n_heads) * k_hs), sub);
     return ldg16(v + (I(t) * v_ts + I(uu - n_heads - n_kv_heads) * v_hs + I(sub * E)));
   };
-  const int tstride = gridDim.x * tpb;
   int t = blockIdx.x * tpb + tok_off;
   // position and slot of the next token are fetched one token ahead
   int pos_n = t < num_tokens ? __ldg(positions + t) : 0;
@@ -235,10 +322,15 @@ cudaError_t launch_typed(const void* q, int64_t q_ts, int64_t q_hs, const void* 
                          cudaStream_t stream) {
   constexpr int L = D / (16 / int(sizeof(T)));
   constexpr int S = kThreads / L;
-  const int units = n_heads + 2 * n_kv_heads;
+  constexpr int ROW = D * int(sizeof(T));
+  const int units_vt = n_heads + n_kv_heads;
+  const int64_t tpb_vt = units_vt <= S ? S / units_vt : 1;
+  const bool vt = tpb_vt * n_kv_heads * ROW <= kVStageMax;
+  const int units = vt ? units_vt : n_heads + 2 * n_kv_heads;
   const int64_t tpb = units <= S ? S / units : 1;
+  const size_t vsmem = vt ? size_t(kVStages) * tpb * n_kv_heads * ROW + kVStages * 8 : 0;
   int64_t blocks = (num_tokens + tpb - 1) / tpb;
-  const int64_t cap = int64_t(device_sm_count()) * 3 * 8;  // 8 waves of 3 resident CTAs per SM, then token-stride
+  const int64_t cap = int64_t(device_sm_count()) * kCtasPerSm * 8;  // 8 waves, then token-stride
   if (blocks > cap) blocks = cap;
   int block_shift = -1;  // page size a power of two: slot / block_size as a shift
   for (int b = 0; b < 31; ++b)
@@ -248,17 +340,18 @@ cudaError_t launch_typed(const void* q, int64_t q_ts, int64_t q_hs, const void* 
   const int64_t widest = std::max({span(q_ts, q_hs, n_heads), span(k_ts, k_hs, n_kv_heads), span(v_ts, v_hs, n_kv_heads),
                                    int64_t(n_heads) * num_tokens * D, num_blocks * n_kv_heads * block_size * D,
                                    int64_t(rope_rows) * D});
-#define FVB_QKN_LAUNCH(I)                                                                                              \
-  qk_norm_rope_store_kernel<T, D, I><<<unsigned(blocks), kThreads, 0, stream>>>(                                      \
+#define FVB_QKN_LAUNCH(I, VTF)                                                                                         \
+  qk_norm_rope_store_kernel<T, D, I, VTF><<<unsigned(blocks), kAllThreads, vsmem, stream>>>(                          \
       static_cast<const T*>(q), I(q_ts), I(q_hs), static_cast<const T*>(k), I(k_ts), I(k_hs),                         \
       static_cast<const T*>(v), I(v_ts), I(v_hs), static_cast<const T*>(q_w), static_cast<const T*>(k_w), eps,       \
       static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), rope_rows, positions, slot_mapping,                \
       int(num_tokens), n_heads, n_kv_heads, static_cast<T*>(q_out), static_cast<T*>(k_pool), static_cast<T*>(v_pool), \
       num_blocks * block_size, block_size, block_shift, err)
-  if (widest < (int64_t(1) << 31)) {
-    FVB_QKN_LAUNCH(int);
+  const bool narrow = widest < (int64_t(1) << 31);
+  if (vt) {
+    if (narrow) FVB_QKN_LAUNCH(int, true); else FVB_QKN_LAUNCH(int64_t, true);
   } else {
-    FVB_QKN_LAUNCH(int64_t);
+    if (narrow) FVB_QKN_LAUNCH(int, false); else FVB_QKN_LAUNCH(int64_t, false);
   }
 #undef FVB_QKN_LAUNCH
   return cudaGetLastError();
