@@ -905,7 +905,7 @@ def _add_blocks(ctx, line, blocks):
             "tokens_per_gpu": g[0]["tokens"],
             "value": _r(sum(x["bytes"] for x in g) / (t * 1e-3) / 1e9, 1), "ms_per_step": _r(t),
             "sustained_ms_per_step": _r(max(x["ms_median"] for x in g)),
-            "roofline": {"kernel": "qk_norm_rope_store_kernel", "bound": "hbm", "achieved": _r(ach, 1), "peak": hbm,
+            "roofline": {"kernel": "qk_norm_rope_ws_kernel", "bound": "hbm", "achieved": _r(ach, 1), "peak": hbm,
                          "unit": "GB/s", "frac": _r(ach / hbm, 4), "traffic": _profile_traffic("qk_norm_rope_config3")},
             "clocks": g[0]["clocks"], "gpu_launches": args.steps,
         }

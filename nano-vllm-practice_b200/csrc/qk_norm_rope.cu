@@ -313,6 +313,230 @@ __global__ void __launch_bounds__(kAllThreads, kCtasPerSm) qk_norm_rope_store_ke
   }
 }
 
+// Rotary pairs of a row staged in shared memory (the split of ldg_pair).
+template <typename T, int D>
+__device__ __forceinline__ uint4 lds_pair(uint32_t row, int sub) {
+  uint32_t a, b, c, d;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(row + sub * 8));
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(c), "=r"(d) : "r"(row + D * int(sizeof(T)) / 2 + sub * 8));
+  return make_uint4(a, b, c, d);
+}
+
+// Warp-specialised kernel (the default path): small blocks of kWsQkThreads q / k threads plus
+// one copy warp, kWsCtasPerSm of them per SM.  The copy warp streams every row of a block
+// pass (the q, k and v rows of its tokens) into a kWsStages-deep shared-memory ring with
+// bulk copies (one per tensor and token when its heads are contiguous); the q / k threads
+// wait on the pass's full barrier, compute from shared memory and release the stage (one
+// arrival per warp); the copy warp stores the value rows from the stage to their pool
+// slots.  No register holds a row in flight and no block-wide barrier orders the passes,
+// so each SM keeps 8 x 3 passes of rows (192 KB at 32 heads x 256 bytes) streaming.
+// Measured on 65k tokens of Hq 16 / Hkv 8 (bf16, D 128), same-box A/B: 6.06-6.11 TB/s
+// against 4.93-5.02 for qk_norm_rope_store_kernel with its copy warp (blocks of 192
+// q / k threads, 4 per SM); blocks of 128 q / k threads at 6 per SM 5.69-5.87, of 32 at 12
+// per SM 5.72-5.89, of 192 at 4 per SM 5.37-5.41.
+constexpr int kWsQkThreads = 64;
+constexpr int kWsThreads = kWsQkThreads + 32;
+constexpr int kWsCtasPerSm = 8;
+constexpr int kWsStages = 3;
+constexpr int kWsSmemMax = 200 * 1024;  // larger passes (over ~66 KB of rows) take the other kernel
+
+template <typename T, int D, typename I>
+__global__ void __launch_bounds__(kWsThreads, kWsCtasPerSm) qk_norm_rope_ws_kernel(
+    const T* __restrict__ q, I q_ts, I q_hs, const T* __restrict__ k, I k_ts, I k_hs,
+    const T* __restrict__ v, I v_ts, I v_hs, const T* __restrict__ q_w, const T* __restrict__ k_w,
+    float eps, const T* __restrict__ cos_t, const T* __restrict__ sin_t, int rope_rows,
+    const int32_t* __restrict__ positions, const int64_t* __restrict__ slot_mapping, int num_tokens,
+    int n_heads, int n_kv_heads, T* __restrict__ q_out, T* __restrict__ k_pool, T* __restrict__ v_pool,
+    int64_t num_slots, int block_size, int block_shift, int* __restrict__ err) {
+  constexpr int E = 16 / int(sizeof(T));
+  constexpr int L = D / E;
+  constexpr int HALF = L / 2;
+  constexpr int S = kWsQkThreads / L;
+  constexpr int ROW = D * int(sizeof(T));
+  extern __shared__ __align__(128) uint8_t wsm[];
+  const int units_qk = n_heads + n_kv_heads;
+  const int units = units_qk + n_kv_heads;  // rows of a token in a stage: q, k, v
+  const int lane = threadIdx.x & 31;
+  const bool packed = units_qk <= S;
+  const int tpb = packed ? S / units_qk : 1;
+  const int tstride = gridDim.x * tpb;
+  const int pass_bytes = tpb * units * ROW;
+  uint64_t* full = reinterpret_cast<uint64_t*>(wsm + kWsStages * pass_bytes);
+  uint64_t* empty = full + kWsStages;
+  const int t_first = blockIdx.x * tpb;
+  const int npass = t_first < num_tokens ? (num_tokens - t_first + tstride - 1) / tstride : 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kWsStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWsQkThreads / 32 + 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (threadIdx.x >= kWsQkThreads) {
+    // ============================== copy warp ==============================
+    auto load_pass = [&](int p) {  // lane 0
+      const int tb = t_first + p * tstride;
+      const int nt = min(tpb, num_tokens - tb);
+      const int st = p % kWsStages;
+      mbar_arrive_expect_tx(&full[st], uint32_t(nt * units * ROW));
+      uint8_t* dst = wsm + st * pass_bytes;
+      for (int i = 0; i < nt; ++i) {
+        const I t = I(tb + i);
+        uint8_t* d = dst + i * units * ROW;
+        if (q_hs == I(D)) {
+          bulk_g2s(d, q + t * q_ts, uint32_t(n_heads * ROW), &full[st]);
+        } else {
+          for (int h = 0; h < n_heads; ++h) bulk_g2s(d + h * ROW, q + t * q_ts + I(h) * q_hs, uint32_t(ROW), &full[st]);
+        }
+        d += n_heads * ROW;
+        if (k_hs == I(D)) {
+          bulk_g2s(d, k + t * k_ts, uint32_t(n_kv_heads * ROW), &full[st]);
+        } else {
+          for (int h = 0; h < n_kv_heads; ++h)
+            bulk_g2s(d + h * ROW, k + t * k_ts + I(h) * k_hs, uint32_t(ROW), &full[st]);
+        }
+        d += n_kv_heads * ROW;
+        if (v_hs == I(D)) {
+          bulk_g2s(d, v + t * v_ts, uint32_t(n_kv_heads * ROW), &full[st]);
+        } else {
+          for (int h = 0; h < n_kv_heads; ++h)
+            bulk_g2s(d + h * ROW, v + t * v_ts + I(h) * v_hs, uint32_t(ROW), &full[st]);
+        }
+      }
+    };
+    if (lane == 0) {
+      for (int p = 0; p < kWsStages - 1 && p < npass; ++p) load_pass(p);
+    }
+    bool ok = true;
+    for (int p = 0; p < npass; ++p) {
+      if (p > 0) {
+        // this warp's value stores of pass p - 1 have read the stage; release it
+        bulk_wait_reads_v();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[(p - 1) % kWsStages]);
+      }
+      const int pn = p + kWsStages - 1;
+      if (lane == 0 && pn < npass) {
+        // the stage of pass pn last held pass p - 1: every warp has released it
+        if (pn >= kWsStages) ok = mbar_wait(&empty[pn % kWsStages], uint32_t(pn / kWsStages - 1) & 1u, err, 0x342);
+        if (ok) load_pass(pn);
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const int st = p % kWsStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[st], uint32_t(p / kWsStages) & 1u, err, 0x343))) break;
+      const int tb = t_first + p * tstride;
+      const int nt = min(tpb, num_tokens - tb);
+      for (int rr = lane; rr < nt * n_kv_heads; rr += 32) {
+        const int i = rr / n_kv_heads, h = rr - i * n_kv_heads;
+        const int64_t slot = __ldg(slot_mapping + tb + i);
+        if (slot < 0 || slot >= num_slots) continue;  // padding, or reported by the q / k threads
+        const int64_t blk = block_shift >= 0 ? (slot >> block_shift) : slot / block_size;
+        const int off = int(slot - blk * block_size);
+        bulk_s2g_v(v_pool + ((I(blk) * n_kv_heads + h) * block_size + off) * I(D),
+                   smem_u32(wsm + st * pass_bytes + (i * units + units_qk + h) * ROW), uint32_t(ROW));
+      }
+      bulk_commit_v();
+    }
+    bulk_wait_done_v();
+    return;
+  }
+
+  // ============================== q / k threads ==============================
+  const int sub = threadIdx.x % L;
+  const int j = threadIdx.x / L;
+  const bool active = !packed || j < tpb * units_qk;  // spare slots still release the stages
+  const int tok_off = packed ? j / units_qk : 0;
+  const int u0 = packed ? j % units_qk : j;
+  const int ustep = packed ? units_qk : S;
+  const uint32_t gmask = L == 32 ? 0xffffffffu : (((1u << L) - 1u) << (lane & ~(L - 1)));
+  const float inv_d = 1.f / float(D);
+  const uint4 wq = ldg_pair<T, D>(q_w, sub), wk = ldg_pair<T, D>(k_w, sub);
+  auto norm_rope = [&](const uint4& raw, const uint4& wv, const uint4& cr, const uint4& sr) -> uint4 {
+    float c[E], sn[E];
+    unpack16<T>(cr, c);
+    unpack16<T>(sr, sn);
+    float x[E], w[E];
+    unpack16<T>(raw, x);
+    unpack16<T>(wv, w);
+    float2 ss2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      const float2 x2 = make_float2(x[e], x[e + 1]);
+      ss2 = __ffma2_rn(x2, x2, ss2);
+    }
+    float ss = ss2.x + ss2.y;
+#pragma unroll
+    for (int o = HALF; o >= 1; o >>= 1) ss += __shfl_xor_sync(gmask, ss, o);
+    const float inv = rsqrtf(ss * inv_d + eps);
+    const float2 inv2 = make_float2(inv, inv);
+    float y[E];
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      const float2 yy = __fmul2_rn(__fmul2_rn(make_float2(x[e], x[e + 1]), inv2), make_float2(w[e], w[e + 1]));
+      y[e] = yy.x;
+      y[e + 1] = yy.y;
+    }
+    float r[E];
+#pragma unroll
+    for (int e = 0; e < E / 2; e += 2) {
+      const float2 ylo = make_float2(y[e], y[e + 1]), yhi = make_float2(y[e + E / 2], y[e + E / 2 + 1]);
+      const float2 lo = __ffma2_rn(ylo, make_float2(c[e], c[e + 1]), __fmul2_rn(yhi, make_float2(-sn[e], -sn[e + 1])));
+      const float2 hi = __ffma2_rn(yhi, make_float2(c[e + E / 2], c[e + E / 2 + 1]),
+                                   __fmul2_rn(ylo, make_float2(sn[e + E / 2], sn[e + E / 2 + 1])));
+      r[e] = lo.x;
+      r[e + 1] = lo.y;
+      r[e + E / 2] = hi.x;
+      r[e + E / 2 + 1] = hi.y;
+    }
+    return pack16<T>(r);
+  };
+  const uint32_t sbase = smem_u32(wsm);
+  int t = t_first + tok_off;
+  int pos_n = t < num_tokens ? __ldg(positions + t) : 0;
+  int64_t slot_n = t < num_tokens ? __ldg(slot_mapping + t) : -1;
+  for (int p = 0; p < npass; ++p, t += tstride) {
+    const int st = p % kWsStages;
+    const bool work = active && t < num_tokens;
+    const int pos = pos_n;
+    int64_t slot = slot_n;
+    if (t + tstride < num_tokens) {
+      pos_n = __ldg(positions + t + tstride);
+      slot_n = __ldg(slot_mapping + t + tstride);
+    }
+    const bool rope_ok = pos >= 0 && pos < rope_rows;
+    uint4 c = make_uint4(0, 0, 0, 0), sn = make_uint4(0, 0, 0, 0);
+    if (work && rope_ok) {
+      c = ldg_pair<T, D>(cos_t + I(pos) * D, sub);
+      sn = ldg_pair<T, D>(sin_t + I(pos) * D, sub);
+    }
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[st], uint32_t(p / kWsStages) & 1u, err, 0x344))) break;
+    if (work) {
+      if (slot >= num_slots) {
+        if (sub == 0) record_error(err, FVB_ERR_BAD_SLOT, t);
+        slot = -1;
+      }
+      if (!rope_ok && u0 == 0 && sub == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, t);
+      const I blk = slot < 0 ? 0 : block_shift >= 0 ? I(slot >> block_shift) : I(slot / block_size);
+      const int off = slot >= 0 ? int(slot - int64_t(blk) * block_size) : 0;
+      const uint32_t tok_row = sbase + uint32_t(st * pass_bytes + tok_off * units * ROW);
+      for (int uu = u0; uu < units_qk; uu += ustep) {
+        const uint4 raw = lds_pair<T, D>(tok_row + uu * ROW, sub);
+        if (uu < n_heads) {
+          if (rope_ok) st_pair<T, D>(q_out + (I(uu) * num_tokens + t) * D, sub, norm_rope(raw, wq, c, sn));
+        } else if (rope_ok && slot >= 0) {
+          st_pair<T, D>(k_pool + ((blk * n_kv_heads + (uu - n_heads)) * block_size + off) * I(D), sub,
+                        norm_rope(raw, wk, c, sn));
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+}
+
 template <typename T, int D>
 cudaError_t launch_typed(const void* q, int64_t q_ts, int64_t q_hs, const void* k, int64_t k_ts, int64_t k_hs,
                          const void* v, int64_t v_ts, int64_t v_hs, const void* q_w, const void* k_w, float eps,
@@ -348,6 +572,29 @@ cudaError_t launch_typed(const void* q, int64_t q_ts, int64_t q_hs, const void* 
       int(num_tokens), n_heads, n_kv_heads, static_cast<T*>(q_out), static_cast<T*>(k_pool), static_cast<T*>(v_pool), \
       num_blocks * block_size, block_size, block_shift, err)
   const bool narrow = widest < (int64_t(1) << 31);
+  constexpr int kWsS = kWsQkThreads / L;
+  const int64_t ws_tpb = units_vt <= kWsS ? kWsS / units_vt : 1;
+  const int64_t ws_pass = ws_tpb * (n_heads + 2 * n_kv_heads) * ROW;
+  const size_t wsmem = size_t(kWsStages) * ws_pass + 2 * kWsStages * 8;
+  if (wsmem <= size_t(kWsSmemMax)) {
+    int64_t wblocks = (num_tokens + ws_tpb - 1) / ws_tpb;
+    const int64_t wcap = int64_t(device_sm_count()) * kWsCtasPerSm * 8;  // 8 waves, then token-stride
+    if (wblocks > wcap) wblocks = wcap;
+#define FVB_QKN_WS(I)                                                                                                  \
+  do {                                                                                                                 \
+    cudaError_t ce = set_smem_once<qk_norm_rope_ws_kernel<T, D, I>>(kWsSmemMax);                                     \
+    if (ce != cudaSuccess) return ce;                                                                                  \
+    qk_norm_rope_ws_kernel<T, D, I><<<unsigned(wblocks), kWsThreads, wsmem, stream>>>(                               \
+        static_cast<const T*>(q), I(q_ts), I(q_hs), static_cast<const T*>(k), I(k_ts), I(k_hs),                       \
+        static_cast<const T*>(v), I(v_ts), I(v_hs), static_cast<const T*>(q_w), static_cast<const T*>(k_w), eps,     \
+        static_cast<const T*>(cos_t), static_cast<const T*>(sin_t), rope_rows, positions, slot_mapping,              \
+        int(num_tokens), n_heads, n_kv_heads, static_cast<T*>(q_out), static_cast<T*>(k_pool),                       \
+        static_cast<T*>(v_pool), num_blocks * block_size, block_size, block_shift, err);                             \
+  } while (0)
+    if (narrow) FVB_QKN_WS(int); else FVB_QKN_WS(int64_t);
+#undef FVB_QKN_WS
+    return cudaGetLastError();
+  }
   if (vt) {
     if (narrow) FVB_QKN_LAUNCH(int, true); else FVB_QKN_LAUNCH(int64_t, true);
   } else {
