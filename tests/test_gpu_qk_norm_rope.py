@@ -99,7 +99,9 @@ def test_golden_norm_rope_store(name, dtype, cuda_device):
     _compare_pools(kp, vp, kp_ref, vp_ref, kp_before, slots, dtype)
 
 
-SHAPES = [(16, 8, 128), (32, 8, 128), (8, 8, 64), (8, 1, 64), (4, 2, 128)]
+# (128, 8, 128): a block pass of 144 rows; in fp32 its three staged passes (216 KB) exceed the
+# warp-specialised kernel's shared-memory limit, so that case runs the other kernel.
+SHAPES = [(16, 8, 128), (32, 8, 128), (8, 8, 64), (8, 1, 64), (4, 2, 128), (128, 8, 128)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"hq{s[0]}_hkv{s[1]}_d{s[2]}")
