@@ -420,12 +420,15 @@ __global__ void __launch_bounds__(kCmbThreads) decode_combine_kernel(const float
   __shared__ float4 g_acc[kGroups][kLanes];
   __shared__ float g_m[kGroups], g_l[kGroups];
   const int b = blockIdx.x / n_heads, head = blockIdx.x % n_heads;
-  // kv_lens was written before the split kernel started, so it is read before the wait.
+  // kv_lens was written before the split kernel started (read before the wait).
   const int kv_len = min(max(__ldg(kv_lens + b), 0), kv_cap);
   const int npages = (kv_len + kPageSize - 1) / kPageSize;
   const int nsplits = (npages + pages_per_split - 1) / pages_per_split;
-  if (nsplits <= 1) return;  // written directly by the split kernel
+  // Every CTA waits for the split grid, also those with nothing to merge: the combine grid
+  // then completes after the split kernel, so work queued behind it on the stream sees the
+  // rows the split kernel wrote directly.
   grid_dependency_wait();
+  if (nsplits <= 1) return;  // written directly by the split kernel
   const int g = threadIdx.x / kLanes, c = threadIdx.x % kLanes;
   const int64_t base = (int64_t(b) * n_heads + head) * max_splits;
   const float4* src = reinterpret_cast<const float4*>(ws_o + base * D) + c;
