@@ -714,7 +714,8 @@ def line_prefill(ctx, g, workload, config):
         "gbs_kv_unique": _r(sum(x["kv_bytes_unique"] for x in g) / (t * 1e-3) / 1e9, 1),
         "flops_per_step_per_gpu": r0["flops"],
         "roofline": {
-            "kernel": "prefill_plan_kernel + prefill_tc_kernel (one paged_attention_gemm call)",
+            "kernel": ("prefill_plan_kernel + prefill_tc_kernel + decode_split_kernel + decode_combine_kernel (one "
+                       "paged_attention_gemm call; the decode kernels take its single-token sequences)"),
             "bound": "tensor", "achieved": _r(ach, 1), "peak": ctx.tflops_peak, "unit": "TFLOP/s",
             "frac": _r(ach / ctx.tflops_peak, 4),
             "peak_source": f"{ctx.peak_src} burst (MEASURED_PEAKS.json bf16_tflops): the first block of K calls",
@@ -725,7 +726,9 @@ def line_prefill(ctx, g, workload, config):
         },
         "e2e": _e2e(g, "flops", "TFLOP/s", 1e12),
         "clocks": g[0]["clocks"],
-        "gpu_launches": 2 * ctx.args.steps,
+        # plan + tensor-core kernel + split-KV decode (single-token sequences; it exits at once when there are
+        # none) + its combine (the workload's block tables span more than one split)
+        "gpu_launches": 4 * ctx.args.steps,
     }
     out["e2e"]["api"] = ("femtovllm_b200.ops.paged_attention_gemm: q and the step metadata copied in from pinned "
                          "host memory, the output copied back, every step (the K/V pools stay resident)")
@@ -858,7 +861,7 @@ def _add_blocks(ctx, line, blocks):
         line["mixed_config4"] = line_prefill(
             ctx, blocks["mixed_config4"], "mixed_config4",
             {"requests_per_gpu": 32, "decode": 24, "prefill": "8 x 512-token chunks", "shared_prefix": 4096,
-             "suffix": "U[64,1024]", "n_heads": 32, "n_kv_heads": 8, "head_dim": 128, "launches": "one",
+             "suffix": "U[64,1024]", "n_heads": 32, "n_kv_heads": 8, "head_dim": 128, "launches": "one call",
              "scaling": "weak"})
     if "long_config5" in blocks:
         g = blocks["long_config5"]

@@ -116,9 +116,18 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     const uint8_t* __restrict__ v_pool, int64_t num_blocks, int n_kv_heads, int num_seqs,
     const int32_t* __restrict__ block_tables, int max_blocks_per_seq, const int32_t* __restrict__ kv_lens,
     int kv_cap, int pages_per_split, int max_splits, float* __restrict__ ws_o, float* __restrict__ ws_lse,
-    const QOLayout lay, int group, int chunks, int* __restrict__ err) {
+    const QOLayout lay, int group, int chunks, const int32_t* __restrict__ q_index,
+    const int32_t* __restrict__ q_pos, int* __restrict__ err) {
   using Tr = DecodeTraits<T, D, NREP>;
   launch_dependents();  // the combine may take free SM slots once every split CTA is resident
+  if (blockIdx.x == gridDim.x - 1 && blockIdx.y == gridDim.y - 1 && blockIdx.z == gridDim.z - 1) {
+    // Launched as a programmatic dependent of the tensor-core prefill kernel (single-token
+    // rows of a prefill batch, which read nothing that kernel writes): the other CTAs run
+    // on the SMs its tail frees, and this one holds the grid open until that kernel has
+    // completed, so whatever waits for this grid (the combine, the next launch on the
+    // stream) also sees the prefill rows.  A no-op in an ordinary launch.
+    grid_dependency_wait();
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   T* qs = reinterpret_cast<T*>(smem + Tr::kOffQ);
@@ -134,12 +143,22 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
   const int n_heads = n_kv_heads * group;
   const int head0 = kvh * group + chunk * NREP;       // query head of row r = head0 + r
   const int nvh = min(NREP, group - chunk * NREP);    // rows that are real heads
+  int tok = b;  // q / out row of sequence b
+  if (q_index != nullptr) {
+    // Single-token sequences of a prefill batch (q_index = its cu_seqlens): sequence b's
+    // query is row q_index[b] at position q_pos[row], which sees keys 0 .. position (the
+    // tensor-core prefill kernel's mask, position clamped to [0, kv_len - 1]); the other
+    // sequences belong to that kernel.
+    tok = __ldg(q_index + b);
+    if (__ldg(q_index + b + 1) - tok != 1) return;
+  }
   int kv_len = max(__ldg(kv_lens + b), 0);
   if (kv_len > kv_cap) {
     // Longer than max_kv_len or than the block table row: never read past either.
     if (split == 0 && threadIdx.x == 0) record_error(err, FVB_ERR_INVALID_ARGUMENT, b);
     kv_len = kv_cap;
   }
+  if (q_index != nullptr && kv_len > 0) kv_len = min(kv_len, max(__ldg(q_pos + tok), 0) + 1);
   const int npages = (kv_len + kPageSize - 1) / kPageSize;
   const int nsplits = (npages + pages_per_split - 1) / pages_per_split;
   const int page_begin = split * pages_per_split;
@@ -149,7 +168,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     if (split == 0) {
       for (int e = threadIdx.x; e < nvh * D; e += blockDim.x) {
         const int r = e / D, d = e % D;
-        out[int64_t(b) * lay.o_ts + int64_t(head0 + r) * lay.o_hs + d] = Elem<T>::from_f(0.f);
+        out[int64_t(tok) * lay.o_ts + int64_t(head0 + r) * lay.o_hs + d] = Elem<T>::from_f(0.f);
       }
     }
     return;
@@ -169,7 +188,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
   // 8 (16-bit) dims; the log2-domain scale is applied to the finished dot product.
   for (int e = threadIdx.x; e < NREP * D; e += blockDim.x) {
     const int r = e / D, d = e % D;
-    qs[e] = q[int64_t(b) * lay.q_ts + int64_t(head0 + min(r, nvh - 1)) * lay.q_hs + d];
+    qs[e] = q[int64_t(tok) * lay.q_ts + int64_t(head0 + min(r, nvh - 1)) * lay.q_hs + d];
   }
   const float qk_scale = kLog2e * rsqrtf(float(D));
   __syncthreads();
@@ -373,7 +392,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_split_kernel(
     if (r >= nvh) continue;
     const int head = head0 + r;
     if (nsplits == 1) {
-      out[int64_t(b) * lay.o_ts + int64_t(head) * lay.o_hs + d] = Elem<T>::from_f(O / L);
+      out[int64_t(tok) * lay.o_ts + int64_t(head) * lay.o_hs + d] = Elem<T>::from_f(O / L);
     } else {
       const int64_t idx = (int64_t(b) * n_heads + head) * max_splits + split;
       ws_o[idx * D + d] = O / L;
@@ -414,21 +433,30 @@ __global__ void __launch_bounds__(kCmbThreads) decode_combine_kernel(const float
                                                                      T* __restrict__ out,
                                                                      const int32_t* __restrict__ kv_lens, int kv_cap,
                                                                      int num_seqs, int n_heads, int pages_per_split,
-                                                                     int max_splits, const QOLayout lay) {
+                                                                     int max_splits, const QOLayout lay,
+                                                                     const int32_t* __restrict__ q_index,
+                                                                     const int32_t* __restrict__ q_pos) {
   constexpr int kLanes = D / 4;                  // threads per partial row
   constexpr int kGroups = kCmbThreads / kLanes;  // rows per pass: 8 (D 128) or 16 (D 64)
   __shared__ float4 g_acc[kGroups][kLanes];
   __shared__ float g_m[kGroups], g_l[kGroups];
   const int b = blockIdx.x / n_heads, head = blockIdx.x % n_heads;
   // kv_lens was written before the split kernel started (read before the wait).
-  const int kv_len = min(max(__ldg(kv_lens + b), 0), kv_cap);
+  int kv_len = min(max(__ldg(kv_lens + b), 0), kv_cap);
+  int tok = b;
+  bool merge = true;
+  if (q_index != nullptr) {  // as in the split kernel: single-token sequences of a prefill batch
+    tok = __ldg(q_index + b);
+    merge = __ldg(q_index + b + 1) - tok == 1;
+    if (merge && kv_len > 0) kv_len = min(kv_len, max(__ldg(q_pos + tok), 0) + 1);
+  }
   const int npages = (kv_len + kPageSize - 1) / kPageSize;
   const int nsplits = (npages + pages_per_split - 1) / pages_per_split;
   // Every CTA waits for the split grid, also those with nothing to merge: the combine grid
   // then completes after the split kernel, so work queued behind it on the stream sees the
   // rows the split kernel wrote directly.
   grid_dependency_wait();
-  if (nsplits <= 1) return;  // written directly by the split kernel
+  if (!merge || nsplits <= 1) return;  // written directly by the split kernel (or not a row of ours)
   const int g = threadIdx.x / kLanes, c = threadIdx.x % kLanes;
   const int64_t base = (int64_t(b) * n_heads + head) * max_splits;
   const float4* src = reinterpret_cast<const float4*>(ws_o + base * D) + c;
@@ -487,14 +515,14 @@ __global__ void __launch_bounds__(kCmbThreads) decode_combine_kernel(const float
     O.z = fmaf(a.z, w, O.z);
     O.w = fmaf(a.w, w, O.w);
   }
-  store4(out + int64_t(b) * lay.o_ts + int64_t(head) * lay.o_hs + 4 * c,
+  store4(out + int64_t(tok) * lay.o_ts + int64_t(head) * lay.o_hs + 4 * c,
          make_float4(O.x / L, O.y / L, O.z / L, O.w / L));
 }
 
 template <typename T, int D>
 cudaError_t launch_combine_t(const float* ws_o, const float* ws_lse, void* out, const int32_t* kv_lens, int kv_cap,
                              int num_seqs, int n_heads, int pages_per_split, int max_splits, const QOLayout& lay,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, const int32_t* q_index = nullptr, const int32_t* q_pos = nullptr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(num_seqs) * unsigned(n_heads));
   cfg.blockDim = dim3(kCmbThreads);
@@ -506,15 +534,17 @@ cudaError_t launch_combine_t(const float* ws_o, const float* ws_lse, void* out, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, D>, ws_o, ws_lse, static_cast<T*>(out), kv_lens, kv_cap,
-                            num_seqs, n_heads, pages_per_split, max_splits, lay);
+                            num_seqs, n_heads, pages_per_split, max_splits, lay, q_index, q_pos);
 }
 
 template <typename T, int D, int NREP>
 cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const void* v_pool, int64_t num_blocks,
                             int n_kv_heads, int num_seqs, const int32_t* block_tables, int max_blocks_per_seq,
                             const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan, const QOLayout& lay,
-                            int group, void* workspace, int* err, cudaStream_t stream) {
+                            int group, void* workspace, int* err, cudaStream_t stream, const int32_t* q_index,
+                            const int32_t* q_pos) {
   using Tr = DecodeTraits<T, D, NREP>;
+  const bool after_prefill = q_index != nullptr;  // programmatic dependent of the prefill kernel
   const int kv_cap = int(std::min<int64_t>(std::min<int64_t>(max_kv_len, int64_t(max_blocks_per_seq) * kPageSize),
                                            int64_t(plan.max_splits) * plan.pages_per_split * kPageSize));
   CUtensorMap kmap;
@@ -535,24 +565,34 @@ cudaError_t launch_decode_t(const void* q, void* out, const void* k_pool, const 
     ws_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((o_bytes + 255) & ~size_t(255)));
   }
   const int chunks = (group + NREP - 1) / NREP;
-  dim3 grid(plan.max_splits, n_kv_heads * chunks, num_seqs);
-  kern<<<grid, kDecodeThreads, Tr::kSmemBytes, stream>>>(
-      kmap, static_cast<const T*>(q), static_cast<T*>(out), static_cast<const uint8_t*>(v_pool), num_blocks,
-      n_kv_heads, num_seqs, block_tables, max_blocks_per_seq, kv_lens, kv_cap, plan.pages_per_split, plan.max_splits,
-      ws_o, ws_lse, lay, group, chunks, err);
-  ce = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.max_splits, n_kv_heads * chunks, num_seqs);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = Tr::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = after_prefill ? 1 : 0;
+  ce = cudaLaunchKernelEx(&cfg, kern, kmap, static_cast<const T*>(q), static_cast<T*>(out),
+                          static_cast<const uint8_t*>(v_pool), num_blocks, n_kv_heads, num_seqs, block_tables,
+                          max_blocks_per_seq, kv_lens, kv_cap, plan.pages_per_split, plan.max_splits, ws_o, ws_lse,
+                          lay, group, chunks, q_index, q_pos, err);
+  if (ce == cudaSuccess) ce = cudaGetLastError();
   if (ce != cudaSuccess || plan.max_splits <= 1) return ce;
   return launch_combine_t<T, D>(ws_o, ws_lse, out, kv_lens, kv_cap, num_seqs, n_kv_heads * group,
-                                plan.pages_per_split, plan.max_splits, lay, stream);
+                                plan.pages_per_split, plan.max_splits, lay, stream, q_index, q_pos);
 }
 
 template <typename T, int D>
 cudaError_t dispatch_nrep(int nrep, const void* q, void* out, const void* k_pool, const void* v_pool,
                           int64_t num_blocks, int n_kv_heads, int num_seqs, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, const DecodePlan& plan,
-                          const QOLayout& lay, void* ws, int* err, cudaStream_t stream) {
+                          const QOLayout& lay, void* ws, int* err, cudaStream_t stream, const int32_t* q_index,
+                          const int32_t* q_pos) {
 #define FVB_DT_ARGS q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables, max_blocks_per_seq, \
-                    kv_lens, max_kv_len, plan, lay, nrep, ws, err, stream
+                    kv_lens, max_kv_len, plan, lay, nrep, ws, err, stream, q_index, q_pos
   switch (decode_tile_heads(nrep)) {
     case 1:
       return launch_decode_t<T, D, 1>(FVB_DT_ARGS);
@@ -600,11 +640,11 @@ cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const vo
                           int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
                           const DecodePlan& plan, const QOLayout& lay, void* workspace, int* err,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const int32_t* q_index, const int32_t* q_pos) {
   if (num_seqs == 0) return cudaSuccess;
   const int nrep = n_heads / n_kv_heads;
 #define FVB_DECODE_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, block_tables, \
-                        max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, workspace, err, stream
+                        max_blocks_per_seq, kv_lens, max_kv_len, plan, lay, workspace, err, stream, q_index, q_pos
   if (dtype == FVB_DTYPE_BF16) {
     return head_dim == 128 ? dispatch_nrep<__nv_bfloat16, 128>(FVB_DECODE_ARGS)
                            : dispatch_nrep<__nv_bfloat16, 64>(FVB_DECODE_ARGS);

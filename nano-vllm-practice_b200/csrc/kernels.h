@@ -76,11 +76,22 @@ cudaError_t launch_decode(const void* q, void* out, const void* k_pool, const vo
                           int n_heads, int n_kv_heads, int head_dim, int num_seqs, const int32_t* block_tables,
                           int max_blocks_per_seq, const int32_t* kv_lens, int max_kv_len, int dtype,
                           const DecodePlan& plan, const QOLayout& lay, void* workspace, int* err,
-                          cudaStream_t stream);
+                          cudaStream_t stream, const int32_t* q_index = nullptr, const int32_t* q_pos = nullptr);
+// With q_index (a prefill batch's cu_seqlens) and q_pos (its positions), launch_decode
+// serves only the sequences with exactly one query token, row q_index[s] at position
+// q_pos[row], and leaves every other sequence's rows untouched.  That launch is a
+// programmatic dependent of the kernel before it on the stream (the tensor-core prefill
+// kernel, which writes only the other rows) and completes after it.
+
+// Splits of the decode plan that serves a prefill batch's single-token sequences: the
+// prefill workspace reserves partials for this many splits per (sequence, head).
+constexpr int kSingleRowMaxSplits = 16;
 
 struct PrefillPlan {
   int tile_tokens;      // query tokens per tile (128 / GQA group on the tensor-core path)
   int64_t max_tiles;    // upper bound on query tiles over all sequences
+  bool single_rows_apart;  // single-token sequences go to the split-KV decode kernel
+  size_t off_single;       // their split partials in the workspace
   size_t ws_bytes;
 };
 PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int64_t q_len_flatten,
@@ -94,9 +105,11 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
                            cudaStream_t stream);
 
 // One-CTA work plan of the tensor-core prefill kernels (prefill_sm100.cu): sequences by
-// descending kv_len, and the scan of work items of `tiles_per_item` query tiles each.
+// descending kv_len, and the scan of work items of `tiles_per_item` query tiles each
+// (none for single-token sequences when skip_single is set).
 cudaError_t launch_prefill_plan(const int32_t* cu_seqlens, const int32_t* kv_lens, int num_seqs, int tile_tokens,
-                                int tiles_per_item, int32_t* order, int32_t* cu_items, cudaStream_t stream);
+                                int tiles_per_item, int32_t* order, int32_t* cu_items, cudaStream_t stream,
+                                int skip_single = 0);
 
 // Decode on the tensor-core attention kernel (decode mode: token s of sequence s at
 // position kv_len - 1), with split-KV when there are too few (sequence, kv head) CTAs.

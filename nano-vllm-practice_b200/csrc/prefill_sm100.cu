@@ -13,6 +13,9 @@
 // tile well enough that the tensor cores beat the SIMT split-KV decode.  Its
 // items are single query tiles, so the two softmax warpgroups share the one tile
 // and take alternate KV tiles ("interleaved KV", merged in the epilogue).
+// Prefill batches with GQA groups of 1-4 give their single-token sequences no tile
+// here: launch_prefill hands them to the split-KV decode kernel (decode.cu), which
+// runs on the SMs this kernel's last wave frees.
 //
 // Query tile = 128 rows: 128 / n_rep consecutive query tokens of one sequence
 // x the n_rep query heads of one kv head's GQA group, so every K/V byte
@@ -111,12 +114,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 //  order[p]    = p-th sequence by descending kv_len (identity beyond kSortMaxSeqs
 //                sequences), so the longest-context work is dispatched first;
 //  cu_items[p] = exclusive scan of ceil(ceil(q_len / tile_tokens) / tiles_per_item)
-//                (work items of that many query tiles) over that order.
+//                (work items of that many query tiles) over that order; sequences of
+//                one query token get none when skip_single is set (the split-KV decode
+//                kernel serves them).
 __global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __restrict__ cu_seqlens,
                                                             const int32_t* __restrict__ kv_lens, int num_seqs,
                                                             int tile_tokens, int tiles_per_item,
                                                             int32_t* __restrict__ order,
-                                                            int32_t* __restrict__ cu_items) {
+                                                            int32_t* __restrict__ cu_items, int skip_single) {
   __shared__ int kv_sh[kSortMaxSeqs];
   __shared__ int warp_tot[32];
   __shared__ int carry;
@@ -150,7 +155,7 @@ __global__ void __launch_bounds__(1024) prefill_plan_kernel(const int32_t* __res
       const int s = order[p];
       // decode mode (cu_seqlens == nullptr): one query token per sequence
       const int ql = cu_seqlens ? __ldg(cu_seqlens + s + 1) - __ldg(cu_seqlens + s) : 1;
-      const int tiles = ql > 0 ? (ql + tile_tokens - 1) / tile_tokens : 0;
+      const int tiles = ql > 0 && !(skip_single && ql == 1) ? (ql + tile_tokens - 1) / tile_tokens : 0;
       v = (tiles + tiles_per_item - 1) / tiles_per_item;
     }
     int x = v;
@@ -706,7 +711,8 @@ cudaError_t launch_tc(const void* q, void* out, const void* k_pool, const void* 
   if (ce != cudaSuccess) return ce;
   int32_t* order = static_cast<int32_t*>(workspace);
   int32_t* cu_items = order + ((num_seqs + 63) & ~63);
-  ce = launch_prefill_plan(cu_seqlens, kv_lens, num_seqs, TOK, 2, order, cu_items, stream);
+  ce = launch_prefill_plan(cu_seqlens, kv_lens, num_seqs, TOK, 2, order, cu_items, stream,
+                           cu_seqlens != nullptr && plan.single_rows_apart ? 1 : 0);
   if (ce != cudaSuccess) return ce;
   auto kern = prefill_tc_kernel<T, D, NREP, kIlv>;
   ce = set_smem_once<prefill_tc_kernel<T, D, NREP, kIlv>>(C::kSmemBytes);
@@ -754,9 +760,10 @@ cudaError_t dispatch_tc(int nrep, const void* q, void* out, const void* k_pool, 
 }  // namespace
 
 cudaError_t launch_prefill_plan(const int32_t* cu_seqlens, const int32_t* kv_lens, int num_seqs, int tile_tokens,
-                                int tiles_per_item, int32_t* order, int32_t* cu_items, cudaStream_t stream) {
+                                int tiles_per_item, int32_t* order, int32_t* cu_items, cudaStream_t stream,
+                                int skip_single) {
   prefill_plan_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, kv_lens, num_seqs, tile_tokens, tiles_per_item, order,
-                                              cu_items);
+                                              cu_items, skip_single);
   return cudaGetLastError();
 }
 
@@ -776,6 +783,16 @@ PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim
   p.max_tiles = (q_len_flatten + 2 * p.tile_tokens - 1) / (2 * p.tile_tokens) + num_seqs;
   // order[num_seqs] (padded to 64 entries) + cu_items[num_seqs + 1]
   p.ws_bytes = ((size_t((num_seqs + 63) & ~63) + num_seqs + 1) * 4 + 255) & ~size_t(255);
+  // Sequences of one query token (decode rows of a mixed batch) fill 1 / tile_tokens of a
+  // query tile here; with GQA groups of up to 4 they go to the split-KV decode kernel
+  // instead, whose partials (at most kSingleRowMaxSplits splits per row) follow the plan
+  // when they fit in 64 MB.
+  const int group = n_heads / n_kv_heads;
+  const size_t rows = size_t(num_seqs) * n_heads * kSingleRowMaxSplits;
+  const size_t single_bytes = ((rows * head_dim * 4 + 255) & ~size_t(255)) + rows * 4;
+  p.single_rows_apart = group <= 4 && single_bytes <= (size_t(64) << 20);
+  p.off_single = p.ws_bytes;
+  if (p.single_rows_apart) p.ws_bytes += single_bytes;
   return p;
 }
 
@@ -792,13 +809,30 @@ cudaError_t launch_prefill(const void* q, void* out, const void* k_pool, const v
 #define FVB_DISPATCH_ARGS nrep, q, out, k_pool, v_pool, num_blocks, n_kv_heads, num_seqs, q_len_flatten, cu_seqlens, \
                           block_tables, max_blocks_per_seq, kv_lens, kv_cap, positions, plan, lay, 0, 1, nullptr,  \
                           nullptr, workspace, err, stream
+  cudaError_t ce;
   if (dtype == FVB_DTYPE_BF16) {
-    return head_dim == 128 ? dispatch_tc<__nv_bfloat16, 128, false>(FVB_DISPATCH_ARGS)
-                           : dispatch_tc<__nv_bfloat16, 64, false>(FVB_DISPATCH_ARGS);
-  }
-  return head_dim == 128 ? dispatch_tc<__half, 128, false>(FVB_DISPATCH_ARGS)
+    ce = head_dim == 128 ? dispatch_tc<__nv_bfloat16, 128, false>(FVB_DISPATCH_ARGS)
+                         : dispatch_tc<__nv_bfloat16, 64, false>(FVB_DISPATCH_ARGS);
+  } else {
+    ce = head_dim == 128 ? dispatch_tc<__half, 128, false>(FVB_DISPATCH_ARGS)
                          : dispatch_tc<__half, 64, false>(FVB_DISPATCH_ARGS);
+  }
 #undef FVB_DISPATCH_ARGS
+  if (ce != cudaSuccess || !plan.single_rows_apart) return ce;
+  // The split-KV decode kernel takes the single-token sequences (prefill_plan_kernel gave
+  // them no tile), launched as a programmatic dependent of the tensor-core kernel so its
+  // CTAs fill the SMs that kernel's last wave leaves idle.  Its plan is sized for the
+  // block table's capacity, with splits lengthened until there are at most
+  // kSingleRowMaxSplits.
+  DecodePlan dp = plan_decode(num_seqs, n_heads, n_kv_heads, head_dim, kv_cap, device_sm_count());
+  const int max_pages = std::max(1, (kv_cap + kPageSize - 1) / kPageSize);
+  while (dp.max_splits > kSingleRowMaxSplits) {
+    dp.pages_per_split *= 2;
+    dp.max_splits = (max_pages + dp.pages_per_split - 1) / dp.pages_per_split;
+  }
+  return launch_decode(q, out, k_pool, v_pool, num_blocks, n_heads, n_kv_heads, head_dim, num_seqs, block_tables,
+                       max_blocks_per_seq, kv_lens, kv_cap, dtype, dp, lay,
+                       static_cast<uint8_t*>(workspace) + plan.off_single, err, stream, cu_seqlens, positions);
 }
 
 TcDecodePlan plan_tc_decode(int num_seqs, int n_heads, int n_kv_heads, int head_dim, int max_kv_len, int num_sms) {

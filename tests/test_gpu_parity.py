@@ -128,6 +128,33 @@ def test_prefill_sweep(dtype, head_dim, n_rep, case, cuda_device):
     assert_close(out, ref, dtype, f"prefill case{case} {dtype} D{head_dim} rep{n_rep}")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("n_rep", [1, 2, 4, 8])
+def test_prefill_single_token_rows_at_earlier_positions(dtype, head_dim, n_rep, cuda_device):
+    # One-token sequences of a mixed batch whose query sits before the last cached key
+    # (a recomputed token) see keys 0 .. position only, whichever kernel serves them
+    # (groups of 1-4 send them to the split-KV decode kernel, 8 keeps them in tiles).
+    q_lens = np.array([1, 40, 1, 1, 1, 130, 1])
+    kv = np.array([300, 100, 50, 5000, 17, 130, 70000])
+    hkv = 2
+    b = workloads.custom(kv, q_lens, hkv * n_rep, hkv, head_dim, dtype, seed=n_rep).materialize(cuda_device)
+    pos = b.positions.copy()
+    cu = b.cu_seqlens
+    for s, p in [(0, 123), (2, 0), (3, 2047), (4, 16), (6, 65535)]:
+        assert q_lens[s] == 1
+        pos[cu[s]] = p
+    md = b.device_metadata(cuda_device)
+    cabi.read_device_error()
+    out = cabi.prefill(b.q, b.k_pool, b.v_pool, md["cu_seqlens"], b.max_q_len, md["block_tables"], md["kv_lens"],
+                       torch.from_numpy(pos).to(cuda_device))
+    ref = oracle.prefill_attention(b.q.float().cpu().numpy(), b.k_pool.float().cpu().numpy(),
+                                   b.v_pool.float().cpu().numpy(), cu, b.block_tables, b.kv_lens, pos,
+                                   acc_dtype=np.float32)
+    assert_close(out, ref, dtype, f"single-token rows {dtype} D{head_dim} rep{n_rep}")
+    assert cabi.read_device_error() == (0, 0)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_store_kvcache_sweep_bit_exact(dtype, cuda_device):
     b = workloads.custom([40, 1, 17, 300], [40, 1, 9, 100], 8, 4, 128, dtype, seed=3).materialize(cuda_device)
