@@ -114,8 +114,8 @@ FVB_API int fvb_store_kvcache(const void* k, const void* v, int64_t token_stride
  *          reference's in-place division of 16-bit logits does.
  * presence_penalties may be NULL (no penalty); token_table int64 [num_rows][table_stride].
  * rng_state: device uint64[2] {seed, offset}; each launch adds 1 to offset, on the device.
- * workspace: fvb_sample_workspace_size(num_rows, vocab) bytes, 16-byte aligned; its first 4 bytes (a
- * counter) must be zero before the first launch (e.g. cudaMemsetAsync once) and every launch leaves them
+ * workspace: fvb_sample_workspace_size(num_rows, vocab) bytes, 16-byte aligned; its first 4 bytes
+ * (reserved) must be zero before the first launch (e.g. cudaMemsetAsync once) and every launch leaves them
  * zero.
  * Replaces the reference's Python lists, count matrix and per-group launches; no counterpart in its
  * native module.

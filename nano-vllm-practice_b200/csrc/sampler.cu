@@ -23,8 +23,9 @@
 // barrier on that path (only around the presence bitmap of penalised rows, whose words the
 // warps also store for the finish kernel).  sample_finish_kernel, one CTA per row and launched
 // as a programmatic dependent of the first, merges the row's partials, draws the Philox uniform,
-// finds the 2048-column run holding it and rescans only that run for the exact token; the last
-// CTA to finish advances the RNG offset, so a CUDA-graph replay draws fresh numbers.
+// finds the 2048-column run holding it and rescans only that run for the exact token.  The
+// partials kernel's first thread copies the RNG key and offset into the workspace for the finish
+// kernel and advances the offset, so a CUDA-graph replay draws fresh numbers.
 #include <algorithm>
 
 #include "common.cuh"
@@ -71,7 +72,7 @@ struct SampleArgs {
   int64_t* out;
   float2* partials;   // [row][part slot < maxparts][warp][sub-run < maxsub]
   uint32_t* presence; // [row][vocab / 32]: presence bitmaps of penalised rows, for the finish kernel
-  unsigned* ctl;      // {grid ticket, batch-wide penalty flag}
+  unsigned* ctl;      // {unused (zero), batch-wide penalty flag, -, -, this launch's Philox key and offset}
   int64_t vp, per;    // row length rounded up to 256; columns per CTA
   int maxparts, maxsub;  // part slots per row; partials per warp run
   int64_t pwords;        // presence words per row: ceil(vocab / 32)
@@ -476,7 +477,14 @@ __global__ void __launch_bounds__(kThreads, 4) sample_partials_kernel(SampleArgs
   if (a.pens != nullptr)
     for (int r = threadIdx.x; r < a.num_rows; r += kThreads) anyp |= fabsf(__ldg(a.pens + r)) > kPenaltyAbove;
   anyp = __syncthreads_or(anyp);
-  if (blockIdx.x == 0 && threadIdx.x == 0) a.ctl[1] = unsigned(anyp);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    a.ctl[1] = unsigned(anyp);
+    // This launch's Philox key and counter offset, handed to the finish kernel, and the offset
+    // advanced for the next launch (the finish kernel reads only the copy).
+    const unsigned long long seed = __ldcg(a.rng), off = __ldcg(a.rng + 1);
+    *reinterpret_cast<ulonglong2*>(a.ctl + 4) = make_ulonglong2(seed, off);
+    a.rng[1] = off + 1ull;
+  }
   for (int64_t f = f0; f < f1;) {
     const int64_t row = f / a.vp, fe = min(f1, (row + 1) * a.vp);
     const int64_t lo = f - row * a.vp, hi = max(lo, min(fe - row * a.vp, a.vocab));
@@ -514,7 +522,6 @@ struct Shared {
   int red_i[kWarps];
   int flag;
   double target;
-  unsigned long long rng[2];
 };
 
 // One CTA per row: merge the row's partials; greedy rows take the maximum, sampled rows draw.
@@ -526,18 +533,24 @@ __global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int row = blockIdx.x;
   const T* lrow = static_cast<const T*>(a.logits) + int64_t(row) * a.row_stride;
-  if (threadIdx.x == 0) {
-    sm.rng[0] = __ldcg(a.rng);
-    sm.rng[1] = __ldcg(a.rng + 1);
-  }
   const float t_row = __ldg(a.temps + row), p_row = a.pens != nullptr ? __ldg(a.pens + row) : 0.f;
   // Launched as a programmatic dependent of sample_partials_kernel: everything above overlaps its
-  // tail; from here on its partials, flag and presence words are complete and visible.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int anyp = int(__ldcg(a.ctl + 1));
-  const RowMode md = row_mode<T>(a, t_row, p_row, anyp);
+  // tail; after the wait its partials, flag, key copy and presence words are complete and visible.
   const float2* rp = a.partials + int64_t(row) * a.maxparts * kWarps * a.maxsub;
   const int np = parts_of_row(row, a) * kWarps * a.maxsub;
+  constexpr int kRun = 4;
+  const int pp = (np + kThreads - 1) / kThreads;
+  const int k0 = min(int(threadIdx.x) * pp, np), k1 = min(k0 + pp, np);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The flag, the key and (sampled rows) the first partials in one round trip.
+  const unsigned anyp_u = __ldcg(a.ctl + 1);
+  const ulonglong2 key = __ldcg(reinterpret_cast<const ulonglong2*>(a.ctl + 4));
+  float2 run[kRun];
+  if (t_row >= kGreedyBelow) {
+#pragma unroll
+    for (int j = 0; j < kRun; ++j) run[j] = k0 + j < k1 ? __ldcg(rp + k0 + j) : make_float2(-INFINITY, 0.f);
+  }
+  const RowMode md = row_mode<T>(a, t_row, p_row, int(anyp_u));
   if (md.mode == kModeGreedy) {
     float bv = -INFINITY;
     int bi = INT_MAX;
@@ -558,17 +571,10 @@ __global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
       a.out[row] = bi == INT_MAX ? 0 : bi;
     }
   } else {
-    // Each thread a contiguous run of partials (held in registers when short).
-    constexpr int kRun = 4;
-    const int pp = (np + kThreads - 1) / kThreads;
-    const int k0 = min(int(threadIdx.x) * pp, np), k1 = min(k0 + pp, np);
-    float2 run[kRun];
+    // Each thread a contiguous run of partials (the first kRun loaded above).
     float gm = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kRun; ++j) {
-      run[j] = k0 + j < k1 ? __ldcg(rp + k0 + j) : make_float2(-INFINITY, 0.f);
-      gm = fmaxf(gm, run[j].x);
-    }
+    for (int j = 0; j < kRun; ++j) gm = fmaxf(gm, run[j].x);
     for (int k = k0 + kRun; k < k1; ++k) gm = fmaxf(gm, __ldcg(rp + k).x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
@@ -586,8 +592,8 @@ __global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
     for (int k = k0 + kRun; k < k1; ++k) wsum += pweight(__ldcg(rp + k));
     double total;
     const double before = block_exclusive_scan(wsum, sm.warp_sums, &total);
-    const uint4 r = philox4x32_10(make_uint4(unsigned(row), 0u, unsigned(sm.rng[1]), unsigned(sm.rng[1] >> 32)),
-                                  unsigned(sm.rng[0]), unsigned(sm.rng[0] >> 32));
+    const uint4 r = philox4x32_10(make_uint4(unsigned(row), 0u, unsigned(key.y), unsigned(key.y >> 32)),
+                                  unsigned(key.x), unsigned(key.x >> 32));
     const double u = double((uint64_t(r.x) << 21) | (r.y >> 11)) * 0x1p-53;  // [0, 1)
     const double target = u * total;
     // The partial whose interval [before_k, before_k + w_k) holds the target.
@@ -666,13 +672,6 @@ __global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
         }
         a.out[row] = pick;
       }
-    }
-  }
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(a.ctl, 1u) == unsigned(a.num_rows - 1)) {  // every CTA has read the offset
-      a.rng[1] = sm.rng[1] + 1ull;
-      a.ctl[0] = 0u;
     }
   }
 }

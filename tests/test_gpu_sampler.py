@@ -187,9 +187,10 @@ def test_workspace_counters_left_zero_and_reusable():
     ws = torch.zeros(cabi.lib().fvb_sample_workspace_size(B, V), dtype=torch.uint8, device=_dev())
     state = _rng(3)
     first = cabi.sample_tokens(logits, temps, None, None, state, ws)
-    ticket = ws[:4].view(torch.int32)  # the grid ticket that decides who advances the offset
+    reserved = ws[:4].view(torch.int32)  # the workspace's reserved first word
     torch.cuda.synchronize()
-    assert int(ticket.item()) == 0
+    assert int(reserved.item()) == 0
+    assert state.cpu().tolist() == [3, 1]  # one launch advanced the offset by one
     state2 = _rng(3)
     again = cabi.sample_tokens(logits, temps, None, None, state2, ws)
     torch.cuda.synchronize()
