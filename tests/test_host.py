@@ -126,6 +126,19 @@ def test_decode_workspace_plan(lib):
     assert lib.fvb_paged_attention_decode_workspace_size(0, 32, 8, 128, 131072) == 0
 
 
+def test_prefill_workspace_reserves_single_token_partials(lib):
+    # The tile plan: order[num_seqs] padded to 64 entries + cu_items[num_seqs + 1], int32, 256-byte rounded.
+    plan = lambda n: ((-(-n // 64) * 64 + n + 1) * 4 + 255) // 256 * 256  # noqa: E731
+    # GQA 1-4: the single-token sequences' split partials follow (16 splits per (sequence, head)).
+    rows = 32 * 32 * 16
+    single = (rows * 128 * 4 + 255) // 256 * 256 + rows * 4
+    assert lib.fvb_paged_attention_prefill_workspace_size(32, 32, 8, 128, 4120, 512) == plan(32) + single
+    # GQA 8 keeps its decode rows in tensor-core tiles: the plan alone.
+    assert lib.fvb_paged_attention_prefill_workspace_size(32, 64, 8, 128, 4120, 512) == plan(32)
+    # Past 64 MB of partials the single-token sequences stay on the tensor-core kernel as well.
+    assert lib.fvb_paged_attention_prefill_workspace_size(4096, 32, 8, 128, 4096, 1) == plan(4096)
+
+
 def test_torch_extension_mirrors_reference_module():
     from femtovllm_b200 import _C, ops
 
