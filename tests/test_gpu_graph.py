@@ -85,3 +85,38 @@ def test_decode_step_replays_in_a_cuda_graph(B, cuda_device):
         assert torch.equal(got, ref), it
         assert torch.equal(kp_g, st["k_pool"]) and torch.equal(vp_g, st["v_pool"]), it
     del g
+
+
+@pytest.mark.parametrize("n_heads", [32, 64])
+def test_mixed_prefill_replays_in_a_cuda_graph(n_heads, cuda_device):
+    # A unified batch of decode rows and prefill chunks: at GQA 4 the single-token rows run on the
+    # split-KV decode kernel launched as a programmatic dependent of the tensor-core kernel, which a
+    # capture turns into a programmatic edge; at GQA 8 they stay in the tensor-core kernel.
+    q_lens = np.array([1, 64, 1, 1, 200, 1, 33])
+    kv = np.array([700, 64, 3000, 17, 1500, 9000, 100])
+    b = workloads.custom(kv, q_lens, n_heads, 8, 128, torch.bfloat16, seed=n_heads).materialize(cuda_device)
+    md = b.device_metadata(cuda_device)
+    q = b.q.clone()
+
+    def attend():
+        return ops.paged_attention_gemm(q, b.k_pool, b.v_pool, md["cu_seqlens"], b.max_q_len, 32, None, None,
+                                        md["block_tables"], md["kv_lens"], md["positions"])
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            attend()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = attend()
+    for it in range(3):
+        q.copy_((torch.randn_like(q, dtype=torch.float32) * (1 + it)).to(q.dtype))
+        g.replay()
+        torch.cuda.synchronize()
+        got = out.clone()
+        ref = attend()
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), it
+    del g
