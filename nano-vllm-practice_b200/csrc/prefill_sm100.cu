@@ -786,11 +786,11 @@ PrefillPlan plan_prefill(int num_seqs, int n_heads, int n_kv_heads, int head_dim
   // Sequences of one query token (decode rows of a mixed batch) fill 1 / tile_tokens of a
   // query tile here; with GQA groups of up to 4 they go to the split-KV decode kernel
   // instead, whose partials (at most kSingleRowMaxSplits splits per row) follow the plan
-  // when they fit in 64 MB.
+  // when they fit in 64 MB (and the sequences in the decode grid's third dimension).
   const int group = n_heads / n_kv_heads;
   const size_t rows = size_t(num_seqs) * n_heads * kSingleRowMaxSplits;
   const size_t single_bytes = ((rows * head_dim * 4 + 255) & ~size_t(255)) + rows * 4;
-  p.single_rows_apart = group <= 4 && single_bytes <= (size_t(64) << 20);
+  p.single_rows_apart = group <= 4 && single_bytes <= (size_t(64) << 20) && num_seqs <= 65535;
   p.off_single = p.ws_bytes;
   if (p.single_rows_apart) p.ws_bytes += single_bytes;
   return p;
